@@ -1,0 +1,131 @@
+// common.cuh — device helpers shared by the forword-b200 kernels (sm_100a).
+//
+// Inline PTX for the Blackwell data-movement primitives the kernels use:
+// mbarrier phases with transaction counts, 1-D bulk async copies
+// (cp.async.bulk, global -> shared, no multicast), and programmatic
+// dependent launch (griddepcontrol).  Every wait is bounded: on timeout it
+// records an error code in the device error word and returns false, so a
+// kernel can wind down instead of hanging the GPU.
+#pragma once
+#include <cuda_fp16.h>
+#include <cstdint>
+
+namespace fwb {
+
+// Error word bits (device status, read back by the host after a step).
+enum : uint32_t {
+    ERR_NONE = 0,
+    ERR_WAIT_FULL = 1u << 0,    // consumer timed out waiting for a weight stage
+    ERR_WAIT_EMPTY = 1u << 1,   // producer timed out waiting for a free stage
+    ERR_WAIT_DRAIN = 1u << 2,   // producer timed out draining its copies on error
+    ERR_BAD_POS = 1u << 3,      // step position outside the KV cache
+    ERR_BAD_TOKEN = 1u << 4,    // token id outside the vocabulary
+    ERR_ATTN_TIMEOUT = 1u << 5,
+};
+
+// Upper bound on polls of one barrier phase.  With the back-off below this is
+// several seconds, far beyond any legitimate wait inside one decode step.
+constexpr uint32_t kMaxPolls = 1u << 22;
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(
+                     smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile(
+        "{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
+            smem_u32(bar)),
+        "r"(bytes)
+        : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait for `parity` of an mbarrier phase.  Returns false (and sets
+// `code` in *err) when the bound is exceeded or another thread already
+// flagged an error.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t *err,
+                                          uint32_t code) {
+    for (uint32_t i = 0; i < kMaxPolls; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (i > 64) __nanosleep(i < 4096 ? 32 : 256);
+        if ((i & 1023) == 1023 && *(volatile uint32_t *)err) return false;
+    }
+    atomicOr(err, code);
+    return false;
+}
+
+// 1-D bulk copy global -> this CTA's shared memory, completing `bytes` of
+// transaction count on `bar`.  src, dst 16-byte aligned; bytes % 16 == 0.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes,
+                                         uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, "
+        "[%3];" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Programmatic dependent launch.  wait: block until the preceding kernel in
+// the stream has completed and its writes are visible.  launch: allow the
+// next kernel to begin launching (its pre-wait prologue then overlaps us).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Named barrier over the first `nthreads` threads (multiple of 32).
+__device__ __forceinline__ void bar_sync(uint32_t id, uint32_t nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+__device__ __forceinline__ float f16_bits_to_f32(uint32_t h) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(h & 0xffffu)));
+}
+
+__device__ __forceinline__ int dp4a_us(uint32_t a, int32_t b, int c) {
+    // a: 4 unsigned bytes, b: 4 signed bytes
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp4a_uu(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp4a_ss(int32_t a, int32_t b, int c) {
+    int d;
+    asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp4a_su(int32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+}  // namespace fwb

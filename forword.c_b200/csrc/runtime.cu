@@ -1,0 +1,924 @@
+// runtime.cu — device model, per-token launch sequence, CUDA graph, C ABI.
+//
+// transformer_init / transformer_forward of forword.c (transformer.c:14-326)
+// become: upload every tensor once to one HBM arena in its GGUF byte layout,
+// resolve all tensors once (instead of the per-token tensor_find string scans
+// of transformer.c:212-222, attention.c:98-107, ffn.c:59-74), and replay one
+// CUDA graph per token.  The graph holds 5 kernels per layer plus the
+// embedding and the LM head, chained with programmatic dependent launch so
+// that each GEMV's weights stream in while its predecessor finishes.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <functional>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../include/forword_b200.h"
+#include "attention.cuh"
+#include "gemv.cuh"
+#include "gguf_reader.h"
+#include "misc_kernels.cuh"
+
+namespace fwb {
+
+static thread_local std::string g_err;
+static void set_err(const std::string &e) { g_err = e; }
+
+#define CK(x)                                                                            \
+    do {                                                                                 \
+        cudaError_t e_ = (x);                                                            \
+        if (e_ != cudaSuccess) {                                                         \
+            set_err(std::string(#x) + " failed: " + cudaGetErrorString(e_));             \
+            return false;                                                                \
+        }                                                                                \
+    } while (0)
+
+// --------------------------------------------------------------------------
+// kernel selection
+// --------------------------------------------------------------------------
+template <int QT, int MODE, int IN>
+static const void *pick_gemv(bool a4, bool big) {
+    if (big) return a4 ? (const void *)gemv_kernel<QT, MODE, IN, true, 544, 1>
+                       : (const void *)gemv_kernel<QT, MODE, IN, false, 544, 1>;
+    return a4 ? (const void *)gemv_kernel<QT, MODE, IN, true, 288, 2>
+              : (const void *)gemv_kernel<QT, MODE, IN, false, 288, 2>;
+}
+
+template <int QT>
+static const void *pick_gemv_mode(int mode, bool a4, bool big) {
+    switch (mode) {
+    case GM_STORE: return pick_gemv<QT, GM_STORE, IN_PLAIN>(a4, big);
+    case GM_RESID: return pick_gemv<QT, GM_RESID, IN_PLAIN>(a4, big);
+    case GM_QKV: return pick_gemv<QT, GM_QKV, IN_RMSNORM>(a4, big);
+    case GM_SWIGLU: return pick_gemv<QT, GM_SWIGLU, IN_RMSNORM>(a4, big);
+    case GM_LOGITS: return pick_gemv<QT, GM_LOGITS, IN_RMSNORM>(a4, big);
+    default: return nullptr;
+    }
+}
+
+static const void *gemv_fn(int qt, int mode, bool a4, bool big) {
+    switch (qt) {
+    case QT_Q4_0: return pick_gemv_mode<QT_Q4_0>(mode, a4, big);
+    case QT_Q5_0: return pick_gemv_mode<QT_Q5_0>(mode, a4, big);
+    case QT_Q8_0: return pick_gemv_mode<QT_Q8_0>(mode, a4, big);
+    default: return nullptr;
+    }
+}
+
+template <int HD>
+static const void *pick_attn_gq(uint32_t gq) {
+    switch (gq) {
+    case 1: return (const void *)attn_decode_kernel<HD, 1>;
+    case 2: return (const void *)attn_decode_kernel<HD, 2>;
+    case 4: return (const void *)attn_decode_kernel<HD, 4>;
+    case 8: return (const void *)attn_decode_kernel<HD, 8>;
+    default: return nullptr;
+    }
+}
+static const void *attn_fn(uint32_t hd, uint32_t gq) {
+    switch (hd) {
+    case 32: return pick_attn_gq<32>(gq);
+    case 48: return pick_attn_gq<48>(gq);
+    case 64: return pick_attn_gq<64>(gq);
+    case 128: return pick_attn_gq<128>(gq);
+    default: return nullptr;
+    }
+}
+
+static int num_sms(int dev) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n > 0 ? n : 1;
+}
+
+static cudaError_t launch_ex(const void *fn, dim3 grid, dim3 block, size_t smem, cudaStream_t st, void **args,
+                             bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = pdl ? at : nullptr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+// --------------------------------------------------------------------------
+// GEMV launch geometry
+// --------------------------------------------------------------------------
+struct GemvLaunch {
+    const void *fn = nullptr;
+    dim3 grid, block;
+    size_t smem = 0;
+    GemvArgs a{};
+    uint64_t weight_bytes = 0;  // algorithmic bytes streamed per launch
+};
+
+static uint32_t pow2ceil(uint32_t v) {
+    uint32_t p = 1;
+    while (p < v) p <<= 1;
+    return p;
+}
+
+constexpr uint32_t kStageTarget = 24 * 1024;
+constexpr uint32_t kRingBudget = 96 * 1024;
+constexpr uint32_t kMaxSmem = 227 * 1024;
+
+// Fills geometry fields of L.a (w, n_out, K, row_bytes set by the caller).
+static bool plan_gemv(int qt, int mode, int sms, GemvLaunch &L) {
+    GemvArgs &a = L.a;
+    const uint32_t nb = a.K / 32;
+    if (a.K % 32 || nb == 0 || a.n_out == 0) { set_err("gemv: bad shape"); return false; }
+    const bool paired = mode == GM_SWIGLU;
+    a.gran = (mode == GM_QKV || paired) ? (paired ? 1u : 2u) : 1u;
+    if (mode == GM_QKV && a.n_out % 2) { set_err("gemv: odd qkv rows"); return false; }
+    a.U = (nb + 1) / 2;
+    a.Upad = a.U <= 32 ? std::max(8u, pow2ceil(a.U)) : (a.U + 31) / 32 * 32;
+    a.S = std::max(1u, 256u / a.Upad);
+    a.NC = a.S * a.Upad;
+    if (a.NC > 512) { set_err("gemv: input width above 32768 is not supported"); return false; }
+    const bool big = a.NC > 256;
+    const uint32_t units = a.n_out / a.gran;
+    const uint32_t grid = std::max(1u, std::min((uint32_t)sms, units));
+    const uint32_t max_units = (units + grid - 1) / grid;
+    const uint32_t max_loc = max_units * a.gran * (paired ? 2 : 1);
+    uint32_t rps = std::max(1u, kStageTarget / (a.S * a.row_bytes));
+    uint32_t R = rps * a.S;
+    const bool need_even = paired || mode == GM_QKV;
+    if (need_even && (R & 1)) R *= 2;
+    const uint32_t cap = (max_loc + a.S - 1) / a.S * a.S;
+    if (R > cap) {
+        R = cap;
+        if (need_even && (R & 1)) R += a.S;
+    }
+    a.R = R;
+    uint32_t stage;
+    if (paired) {
+        const uint32_t half = ((R / 2) * a.row_bytes + 32 + kStageSlack + 127) / 128 * 128;
+        stage = 2 * half;
+    } else {
+        stage = (R * a.row_bytes + 32 + kStageSlack + 127) / 128 * 128;
+    }
+    a.stage_bytes = stage;
+    const uint32_t n_st = (max_loc + R - 1) / R;
+    uint32_t ns = std::max(2u, std::min((uint32_t)kMaxStages, kRingBudget / stage));
+    ns = std::max(1u, std::min(ns, n_st));
+    while (ns > 1 && kHeaderBytes + ns * stage + 128 > kMaxSmem) --ns;
+    if (kHeaderBytes + ns * stage + 128 > kMaxSmem) { set_err("gemv: stage does not fit shared memory"); return false; }
+    a.NS = ns;
+    const bool a4 = (nb % 2 == 0) && ((uintptr_t)a.w % 4 == 0) && (!a.w2 || (uintptr_t)a.w2 % 4 == 0);
+    L.fn = gemv_fn(qt, mode, a4, big);
+    if (!L.fn) { set_err("gemv: unsupported quant type"); return false; }
+    L.grid = dim3(grid);
+    L.block = dim3(a.NC + 32);
+    L.smem = kHeaderBytes + (size_t)ns * stage + 128;
+    L.weight_bytes = (uint64_t)a.n_out * a.row_bytes * (paired ? 2 : 1);
+    return true;
+}
+
+static bool g_attr_done[64];
+static bool set_smem_attrs(int dev) {
+    if (dev < 0 || dev >= 64) return true;
+    if (g_attr_done[dev]) return true;
+    const int qts[3] = {QT_Q4_0, QT_Q5_0, QT_Q8_0};
+    for (int qt : qts)
+        for (int mode = 0; mode <= GM_LOGITS; ++mode)
+            for (int a4 = 0; a4 < 2; ++a4)
+                for (int big = 0; big < 2; ++big) {
+                    const void *fn = gemv_fn(qt, mode, a4, big);
+                    CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem));
+                }
+    g_attr_done[dev] = true;
+    return true;
+}
+
+// --------------------------------------------------------------------------
+// standalone matvec (quant_matvec / quant_matvec_dev)
+// --------------------------------------------------------------------------
+static bool block_bytes_of(uint32_t type, uint32_t &bb) {
+    switch (type) {
+    case 2: bb = 18; return true;
+    case 6: bb = 22; return true;
+    case 8: bb = 34; return true;
+    default: return false;
+    }
+}
+
+struct DevScratch {
+    uint32_t *err = nullptr;
+};
+static DevScratch g_scratch[64];
+
+static uint32_t *device_err_word(int dev) {
+    if (dev < 0 || dev >= 64) return nullptr;
+    if (!g_scratch[dev].err) {
+        if (cudaMalloc(&g_scratch[dev].err, 16) != cudaSuccess) return nullptr;
+        cudaMemset(g_scratch[dev].err, 0, 16);
+    }
+    return g_scratch[dev].err;
+}
+
+static bool matvec_args_ok(const void *w, size_t w_size, uint32_t type, const void *x, const void *y, size_t in,
+                           size_t out, uint32_t &bb, uint32_t &row_bytes) {
+    // quant_matvec.c:270-289
+    if (!w || !x || !y || in == 0 || out == 0) { set_err("quant_matvec: null pointer or zero size"); return false; }
+    if (!block_bytes_of(type, bb)) { set_err("quant_matvec: unsupported ggml type"); return false; }
+    if (in % 32) { set_err("quant_matvec: input_size not a multiple of 32"); return false; }
+    const uint64_t rb = (uint64_t)(in / 32) * bb;
+    if (rb > UINT32_MAX || out > UINT32_MAX || out > SIZE_MAX / rb || w_size < out * rb) {
+        set_err("quant_matvec: weights smaller than output_size rows");
+        return false;
+    }
+    row_bytes = (uint32_t)rb;
+    return true;
+}
+
+static bool matvec_dev(const void *w, size_t w_size, uint32_t type, const float *x, float *y, size_t in, size_t out,
+                       cudaStream_t st) {
+    uint32_t bb, row_bytes;
+    if (!matvec_args_ok(w, w_size, type, x, y, in, out, bb, row_bytes)) return false;
+    if ((uintptr_t)w % 2) { set_err("quant_matvec_dev: weights must be 2-byte aligned"); return false; }
+    int dev;
+    CK(cudaGetDevice(&dev));
+    if (!set_smem_attrs(dev)) return false;
+    GemvLaunch L;
+    L.a.w = static_cast<const uint8_t *>(w);
+    L.a.n_out = (uint32_t)out;
+    L.a.K = (uint32_t)in;
+    L.a.row_bytes = row_bytes;
+    L.a.x = x;
+    L.a.y = y;
+    L.a.err = device_err_word(dev);
+    if (!L.a.err) { set_err("quant_matvec: device error word allocation failed"); return false; }
+    if (!plan_gemv((int)type, GM_STORE, num_sms(dev), L)) return false;
+    void *args[] = {&L.a};
+    CK(launch_ex(L.fn, L.grid, L.block, L.smem, st, args, false));
+    return true;
+}
+
+// --------------------------------------------------------------------------
+// model
+// --------------------------------------------------------------------------
+struct Mat {
+    const uint8_t *p = nullptr;
+    uint32_t type = 0, rows = 0, cols = 0, row_bytes = 0;
+};
+
+struct LayerW {
+    Mat qkv, o, gate, up, down;
+    const float *attn_norm = nullptr, *ffn_norm = nullptr;
+};
+
+struct Step {
+    std::string name;
+    std::function<cudaError_t(cudaStream_t, bool)> run;
+    uint64_t bytes = 0;  // algorithmic HBM bytes of this launch
+};
+
+}  // namespace fwb
+
+struct fwb_model {
+    int dev = 0;
+    int sms = 1;
+    cudaStream_t st = nullptr;
+    fwb::GgufFile gguf;
+    fwb::ModelConfig cfg;
+    uint32_t kv_ctx = 0;
+    uint8_t *arena = nullptr;
+    fwb::Mat embd, head;
+    const float *out_norm = nullptr;
+    std::vector<fwb::LayerW> layers;
+    float *x = nullptr, *q = nullptr, *att = nullptr, *h = nullptr, *logits = nullptr;
+    float *kc = nullptr, *vc = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
+    float *attn_part = nullptr, *am_val = nullptr;
+    uint32_t *attn_ticket = nullptr, *am_idx = nullptr, *am_ticket = nullptr;
+    uint32_t *step = nullptr, *err = nullptr, *hist = nullptr;
+    uint32_t *h_io = nullptr;     // pinned [8]: step in / status out
+    float *h_logits = nullptr;    // pinned [n_vocab]
+    uint64_t weight_bytes = 0;
+    std::vector<fwb::Step> steps;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    bool use_graph = true, use_pdl = true;
+    std::vector<void *> allocs;
+};
+
+namespace fwb {
+
+static bool dalloc(fwb_model *m, void **p, size_t bytes) {
+    CK(cudaMalloc(p, bytes));
+    m->allocs.push_back(*p);
+    CK(cudaMemset(*p, 0, bytes));
+    return true;
+}
+
+static bool check_mat(const GgufTensor *t, uint32_t rows, uint32_t cols, const char *what, bool allow_f32 = false) {
+    if (!t) { set_err(std::string("missing tensor ") + what); return false; }
+    if (t->n_dims < 1 || t->dims[0] != cols || (t->n_dims >= 2 ? t->dims[1] : 1) != rows) {
+        set_err(std::string("unexpected shape for ") + t->name);
+        return false;
+    }
+    uint32_t v, b;
+    if (!ggml_block(t->type, v, b) || (t->type == 0 && !allow_f32)) {
+        set_err(std::string("unsupported ggml type for ") + t->name);
+        return false;
+    }
+    return true;
+}
+
+static void free_model(fwb_model *m) {
+    if (!m) return;
+    if (m->st) cudaStreamSynchronize(m->st);
+    if (m->exec) cudaGraphExecDestroy(m->exec);
+    if (m->graph) cudaGraphDestroy(m->graph);
+    for (void *p : m->allocs) cudaFree(p);
+    if (m->h_io) cudaFreeHost(m->h_io);
+    if (m->h_logits) cudaFreeHost(m->h_logits);
+    if (m->st) cudaStreamDestroy(m->st);
+    delete m;
+}
+
+// Upload tensor bytes from the mapping to dst through pinned staging.
+static bool upload(const uint8_t *src, uint8_t *dst, uint64_t bytes, uint8_t *stage[2], cudaEvent_t ev[2],
+                   size_t chunk, cudaStream_t st, int &flip) {
+    for (uint64_t off = 0; off < bytes; off += chunk) {
+        const size_t n = (size_t)std::min<uint64_t>(chunk, bytes - off);
+        CK(cudaEventSynchronize(ev[flip]));
+        std::memcpy(stage[flip], src + off, n);
+        CK(cudaMemcpyAsync(dst + off, stage[flip], n, cudaMemcpyHostToDevice, st));
+        CK(cudaEventRecord(ev[flip], st));
+        flip ^= 1;
+    }
+    return true;
+}
+
+static bool build_steps(fwb_model *m);
+
+static bool load_model(fwb_model *m, const char *path, size_t max_ctx) {
+    std::string err;
+    if (!m->gguf.open(path, err)) { set_err("gguf_open: " + err); return false; }
+    if (!m->gguf.config(m->cfg, err)) { set_err("model_config: " + err); return false; }
+    const ModelConfig &c = m->cfg;
+    // transformer.c:43-52
+    if (!max_ctx) max_ctx = c.n_ctx < 4096 ? c.n_ctx : 4096;
+    if (max_ctx > c.n_ctx) max_ctx = c.n_ctx;
+    if (!max_ctx) { set_err("invalid context length"); return false; }
+    m->kv_ctx = (uint32_t)max_ctx;
+    if (c.n_head % c.n_head_kv) { set_err("attention: invalid head configuration"); return false; }
+    const uint32_t E = c.n_embd, F = c.n_ff, hd = c.head_dim, H = c.n_head, KV = c.n_head_kv;
+    if (!attn_fn(hd, H / KV)) { set_err("head_dim / GQA group outside this build"); return false; }
+    if (E % 64 || F % 64 || (H * hd) != E) { set_err("model widths outside this build"); return false; }
+
+    // resolve tensors once
+    const GgufTensor *te = m->gguf.find("token_embd.weight");
+    if (!check_mat(te, c.n_vocab, E, "token_embd.weight", true)) return false;
+    const GgufTensor *tn = m->gguf.find("output_norm.weight");
+    const GgufTensor *th = m->gguf.find("output.weight");
+    if (!th) th = m->gguf.find("lm_head.weight");
+    if (!th) th = te;
+    if (!check_mat(th, c.n_vocab, E, "output.weight")) return false;
+    if (tn && (tn->type != 0 || tn->dims[0] != E)) { set_err("output_norm.weight must be F32 [n_embd]"); return false; }
+    struct LT { const GgufTensor *an, *q, *k, *v, *o, *fn, *g, *u, *d; };
+    std::vector<LT> lt(c.n_layer);
+    for (uint32_t l = 0; l < c.n_layer; ++l) {
+        auto f = [&](const char *s) { return m->gguf.find("blk." + std::to_string(l) + "." + s); };
+        LT &t = lt[l];
+        t = {f("attn_norm.weight"), f("attn_q.weight"), f("attn_k.weight"), f("attn_v.weight"),
+             f("attn_output.weight"), f("ffn_norm.weight"), f("ffn_gate.weight"), f("ffn_up.weight"),
+             f("ffn_down.weight")};
+        if (!t.an || !t.fn || t.an->type != 0 || t.fn->type != 0 || t.an->dims[0] != E || t.fn->dims[0] != E) {
+            set_err("missing or non-F32 norm weights at layer " + std::to_string(l));
+            return false;
+        }
+        if (!check_mat(t.q, H * hd, E, "attn_q") || !check_mat(t.k, KV * hd, E, "attn_k") ||
+            !check_mat(t.v, KV * hd, E, "attn_v") || !check_mat(t.o, E, H * hd, "attn_output") ||
+            !check_mat(t.g, F, E, "ffn_gate") || !check_mat(t.u, F, E, "ffn_up") || !check_mat(t.d, E, F, "ffn_down"))
+            return false;
+        if (t.q->type != t.k->type || t.q->type != t.v->type || t.g->type != t.u->type) {
+            set_err("q/k/v (and gate/up) must share a quant type");
+            return false;
+        }
+    }
+
+    // arena layout: every tensor 256-aligned with 256 bytes of slack; the q,
+    // k, v rows of a layer are adjacent so they form one [q|k|v] matrix.
+    uint64_t off = 256;
+    auto place = [&](uint64_t bytes) {
+        const uint64_t o = off;
+        off = (off + bytes + 256 + 255) / 256 * 256;
+        return o;
+    };
+    struct Pl { const GgufTensor *t; uint64_t off; };
+    std::vector<Pl> plan;
+    const uint64_t o_embd = place(te->bytes);
+    plan.push_back({te, o_embd});
+    uint64_t o_head = o_embd;
+    if (th != te) { o_head = place(th->bytes); plan.push_back({th, o_head}); }
+    uint64_t o_onorm = 0;
+    if (tn) { o_onorm = place(tn->bytes); plan.push_back({tn, o_onorm}); }
+    std::vector<uint64_t> lo(c.n_layer * 8);
+    for (uint32_t l = 0; l < c.n_layer; ++l) {
+        LT &t = lt[l];
+        const uint64_t oq = place(t.q->bytes + t.k->bytes + t.v->bytes);
+        plan.push_back({t.q, oq});
+        plan.push_back({t.k, oq + t.q->bytes});
+        plan.push_back({t.v, oq + t.q->bytes + t.k->bytes});
+        const uint64_t oo = place(t.o->bytes), og = place(t.g->bytes), ou = place(t.u->bytes),
+                       od = place(t.d->bytes), oan = place(t.an->bytes), ofn = place(t.fn->bytes);
+        plan.push_back({t.o, oo}); plan.push_back({t.g, og}); plan.push_back({t.u, ou});
+        plan.push_back({t.d, od}); plan.push_back({t.an, oan}); plan.push_back({t.fn, ofn});
+        uint64_t *L = &lo[l * 8];
+        L[0] = oq; L[1] = oo; L[2] = og; L[3] = ou; L[4] = od; L[5] = oan; L[6] = ofn;
+    }
+    const uint64_t arena_bytes = off + 256;
+    if (!dalloc(m, (void **)&m->arena, arena_bytes)) return false;
+
+    // upload
+    {
+        const size_t chunk = 64u << 20;
+        uint8_t *stage[2] = {nullptr, nullptr};
+        cudaEvent_t ev[2] = {nullptr, nullptr};
+        bool ok = true;
+        if (cudaMallocHost(&stage[0], chunk) != cudaSuccess || cudaMallocHost(&stage[1], chunk) != cudaSuccess ||
+            cudaEventCreateWithFlags(&ev[0], cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&ev[1], cudaEventDisableTiming) != cudaSuccess) {
+            set_err("pinned staging allocation failed");
+            ok = false;
+        }
+        if (ok) {
+            cudaEventRecord(ev[0], m->st);
+            cudaEventRecord(ev[1], m->st);
+        }
+        int flip = 0;
+        for (size_t i = 0; ok && i < plan.size(); ++i)
+            ok = upload(plan[i].t->data, m->arena + plan[i].off, plan[i].t->bytes, stage, ev, chunk, m->st, flip);
+        if (ok && cudaStreamSynchronize(m->st) != cudaSuccess) { set_err("upload failed"); ok = false; }
+        for (int i = 0; i < 2; ++i) {
+            if (stage[i]) cudaFreeHost(stage[i]);
+            if (ev[i]) cudaEventDestroy(ev[i]);
+        }
+        if (!ok) return false;
+    }
+
+    auto mat = [&](const GgufTensor *t, uint64_t o, uint32_t rows, uint32_t cols) {
+        Mat mm;
+        mm.p = m->arena + o;
+        mm.type = t->type;
+        mm.rows = rows;
+        mm.cols = cols;
+        uint32_t v, b;
+        ggml_block(t->type, v, b);
+        mm.row_bytes = cols / v * b;
+        return mm;
+    };
+    m->embd = mat(te, o_embd, c.n_vocab, E);
+    m->head = mat(th, o_head, c.n_vocab, E);
+    m->out_norm = tn ? reinterpret_cast<const float *>(m->arena + o_onorm) : nullptr;
+    m->layers.resize(c.n_layer);
+    for (uint32_t l = 0; l < c.n_layer; ++l) {
+        LT &t = lt[l];
+        uint64_t *L = &lo[l * 8];
+        LayerW &w = m->layers[l];
+        w.qkv = mat(t.q, L[0], (H + 2 * KV) * hd, E);
+        w.o = mat(t.o, L[1], E, H * hd);
+        w.gate = mat(t.g, L[2], F, E);
+        w.up = mat(t.u, L[3], F, E);
+        w.down = mat(t.d, L[4], E, F);
+        w.attn_norm = reinterpret_cast<const float *>(m->arena + L[5]);
+        w.ffn_norm = reinterpret_cast<const float *>(m->arena + L[6]);
+        m->weight_bytes += t.q->bytes + t.k->bytes + t.v->bytes + t.o->bytes + t.g->bytes + t.u->bytes +
+                           t.d->bytes + t.an->bytes + t.fn->bytes;
+    }
+    m->weight_bytes += th->bytes + (tn ? tn->bytes : 0) + m->embd.row_bytes;
+
+    // state
+    const size_t kvn = (size_t)c.n_layer * KV * m->kv_ctx * hd;
+    if (!dalloc(m, (void **)&m->x, E * 4) || !dalloc(m, (void **)&m->q, (size_t)H * hd * 4) ||
+        !dalloc(m, (void **)&m->att, (size_t)H * hd * 4) || !dalloc(m, (void **)&m->h, (size_t)F * 4) ||
+        !dalloc(m, (void **)&m->logits, (size_t)c.n_vocab * 4) || !dalloc(m, (void **)&m->kc, kvn * 4) ||
+        !dalloc(m, (void **)&m->vc, kvn * 4) ||
+        !dalloc(m, (void **)&m->rope_cos, (size_t)m->kv_ctx * (hd / 2) * 4 + 4) ||
+        !dalloc(m, (void **)&m->rope_sin, (size_t)m->kv_ctx * (hd / 2) * 4 + 4) ||
+        !dalloc(m, (void **)&m->step, 64) || !dalloc(m, (void **)&m->err, 16) ||
+        !dalloc(m, (void **)&m->hist, (size_t)m->kv_ctx * 4 + 4) ||
+        !dalloc(m, (void **)&m->am_val, 4096 * 4) || !dalloc(m, (void **)&m->am_idx, 4096 * 4) ||
+        !dalloc(m, (void **)&m->am_ticket, 64) || !dalloc(m, (void **)&m->attn_ticket, 4 * KV + 64))
+        return false;
+    CK(cudaMallocHost(&m->h_io, 64));
+    CK(cudaMallocHost(&m->h_logits, (size_t)c.n_vocab * 4));
+
+    // RoPE tables exactly as rope_precompute (rope.c:6-17), on the host
+    {
+        const size_t half = hd / 2;
+        std::vector<float> cs(m->kv_ctx * half), sn(m->kv_ctx * half);
+        for (size_t p = 0; p < m->kv_ctx; ++p)
+            for (size_t i = 0; i < half; ++i) {
+                const float theta = (float)p / powf(c.rope_freq_base, (float)(2 * i) / (float)hd);
+                cs[p * half + i] = cosf(theta);
+                sn[p * half + i] = sinf(theta);
+            }
+        CK(cudaMemcpy(m->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(m->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+    }
+    return build_steps(m);
+}
+
+static uint32_t attn_splits(const fwb_model *m) {
+    const uint32_t KV = m->cfg.n_head_kv;
+    uint32_t s = (2u * m->sms + KV - 1) / KV;
+    s = std::min(s, std::max(1u, m->kv_ctx / 16));
+    return std::max(1u, s);
+}
+
+// Feeds the greedy token of this step into the next one: step[0] = next
+// token, step[1] = pos + 1, hist[pos] = next token.
+__global__ void fwb_advance_kernel(uint32_t *step, uint32_t *hist) {
+    if (threadIdx.x == 0) {
+        const uint32_t nxt = step[2], pos = step[1];
+        hist[pos] = nxt;
+        step[0] = nxt;
+        step[1] = pos + 1;
+    }
+}
+
+static bool build_steps(fwb_model *m) {
+    const ModelConfig &c = m->cfg;
+    const uint32_t E = c.n_embd, F = c.n_ff, hd = c.head_dim, H = c.n_head, KV = c.n_head_kv;
+    const size_t layer_kv = (size_t)KV * m->kv_ctx * hd;
+    m->steps.clear();
+
+    {  // embedding
+        Step s;
+        s.name = "embed";
+        const Mat e = m->embd;
+        const uint64_t rb = e.row_bytes;
+        uint32_t *step = m->step;
+        float *x = m->x;
+        s.bytes = rb;
+        s.run = [=](cudaStream_t st, bool pdl) {
+            const uint8_t *p = e.p;
+            uint32_t t = e.type, cols = e.cols;
+            uint64_t r = rb;
+            const uint32_t *sp = step;
+            float *xp = x;
+            void *args[] = {&p, &t, &cols, &r, &sp, &xp};
+            return launch_ex((const void *)embed_kernel, dim3(std::min(16u, (cols + 255) / 256)), dim3(256), 0,
+                             st, args, pdl);
+        };
+        m->steps.push_back(std::move(s));
+    }
+
+    auto gemv_step = [&](const std::string &name, int mode, const Mat &w, const Mat *w2, uint32_t n_out,
+                         const float *x, const float *norm_w, float *y, GemvArgs extra) -> bool {
+        GemvLaunch L;
+        L.a = extra;
+        L.a.w = w.p;
+        L.a.w2 = w2 ? w2->p : nullptr;
+        L.a.n_out = n_out;
+        L.a.K = w.cols;
+        L.a.row_bytes = w.row_bytes;
+        L.a.x = x;
+        L.a.norm_w = norm_w;
+        L.a.eps = c.norm_eps;
+        L.a.y = y;
+        L.a.step = m->step;
+        L.a.err = m->err;
+        if (!plan_gemv((int)w.type, mode, m->sms, L)) return false;
+        Step s;
+        s.name = name;
+        s.bytes = L.weight_bytes;
+        s.run = [L](cudaStream_t st, bool pdl) {
+            GemvArgs a = L.a;
+            void *args[] = {&a};
+            return launch_ex(L.fn, L.grid, L.block, L.smem, st, args, pdl);
+        };
+        m->steps.push_back(std::move(s));
+        return true;
+    };
+
+    const uint32_t nsplit = attn_splits(m);
+    if (!dalloc(m, (void **)&m->attn_part, (size_t)KV * nsplit * (H / KV) * (hd + 2) * 4)) return false;
+    const void *afn = attn_fn(hd, H / KV);
+
+    for (uint32_t l = 0; l < c.n_layer; ++l) {
+        const LayerW &w = m->layers[l];
+        float *kc = m->kc + l * layer_kv, *vc = m->vc + l * layer_kv;
+        GemvArgs ex{};
+        ex.n_q = H * hd;
+        ex.n_kv = KV * hd;
+        ex.head_dim = hd;
+        ex.kv_ctx = m->kv_ctx;
+        ex.rope_cos = m->rope_cos;
+        ex.rope_sin = m->rope_sin;
+        ex.q_out = m->q;
+        ex.kcache = kc;
+        ex.vcache = vc;
+        const std::string p = "L" + std::to_string(l) + ".";
+        if (!gemv_step(p + "qkv_rope", GM_QKV, w.qkv, nullptr, w.qkv.rows, m->x, w.attn_norm, nullptr, ex))
+            return false;
+        {
+            Step s;
+            s.name = p + "attention";
+            AttnArgs a{};
+            a.q = m->q;
+            a.kc = kc;
+            a.vc = vc;
+            a.out = m->att;
+            a.part = m->attn_part;
+            a.ticket = m->attn_ticket;
+            a.kv_ctx = m->kv_ctx;
+            a.n_split = nsplit;
+            a.scale = 1.0f / sqrtf((float)hd);
+            a.step = m->step;
+            a.err = m->err;
+            s.bytes = 0;  // KV bytes depend on pos; accounted separately
+            s.run = [a, afn, KV, nsplit](cudaStream_t st, bool pdl) {
+                AttnArgs aa = a;
+                void *args[] = {&aa};
+                return launch_ex(afn, dim3(KV, nsplit), dim3(kAttnWarps * 32), 0, st, args, pdl);
+            };
+            m->steps.push_back(std::move(s));
+        }
+        if (!gemv_step(p + "o_proj_resid", GM_RESID, w.o, nullptr, E, m->att, nullptr, m->x, GemvArgs{})) return false;
+        if (!gemv_step(p + "gate_up_swiglu", GM_SWIGLU, w.gate, &w.up, F, m->x, w.ffn_norm, m->h, GemvArgs{}))
+            return false;
+        if (!gemv_step(p + "down_resid", GM_RESID, w.down, nullptr, E, m->h, nullptr, m->x, GemvArgs{})) return false;
+    }
+    {
+        GemvArgs ex{};
+        ex.am_val = m->am_val;
+        ex.am_idx = m->am_idx;
+        ex.ticket = m->am_ticket;
+        ex.out_token = m->step + 2;
+        if (!gemv_step("lm_head_argmax", GM_LOGITS, m->head, nullptr, c.n_vocab, m->x, m->out_norm, m->logits, ex))
+            return false;
+    }
+    // The head GEMV needs a norm weight; a model without output_norm gets the
+    // identity norm (transformer.c:355-357 copies x unnormalised): not supported.
+    if (!m->out_norm) { set_err("output_norm.weight is required by this build"); return false; }
+    {  // advance: step[0] = next token, step[1] = pos + 1, hist[pos] = next
+        Step s;
+        s.name = "advance";
+        uint32_t *step = m->step, *hist = m->hist;
+        s.run = [step, hist](cudaStream_t st, bool pdl) {
+            (void)pdl;
+            uint32_t *a0 = step, *a1 = hist;
+            void *args[] = {&a0, &a1};
+            return launch_ex((const void *)fwb_advance_kernel, dim3(1), dim3(32), 0, st, args, false);
+        };
+        m->steps.push_back(std::move(s));
+    }
+    return true;
+}
+
+static bool run_steps(fwb_model *m) {
+    for (size_t i = 0; i < m->steps.size(); ++i) {
+        cudaError_t e = m->steps[i].run(m->st, m->use_pdl && i > 0);
+        if (e != cudaSuccess) {
+            set_err("launch " + m->steps[i].name + ": " + cudaGetErrorString(e));
+            return false;
+        }
+    }
+    return true;
+}
+
+static bool capture_graph(fwb_model *m) {
+    CK(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal));
+    bool ok = run_steps(m);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(m->st, &g);
+    if (!ok || e != cudaSuccess) {
+        if (g) cudaGraphDestroy(g);
+        if (ok) set_err(std::string("graph capture: ") + cudaGetErrorString(e));
+        return false;
+    }
+    m->graph = g;
+    CK(cudaGraphInstantiate(&m->exec, g, 0));
+    return true;
+}
+
+static bool enqueue_step(fwb_model *m) {
+    if (m->use_graph && m->exec) {
+        CK(cudaGraphLaunch(m->exec, m->st));
+        return true;
+    }
+    return run_steps(m);
+}
+
+static bool finish(fwb_model *m) {
+    CK(cudaMemcpyAsync(m->h_io + 4, m->err, 4, cudaMemcpyDeviceToHost, m->st));
+    CK(cudaMemcpyAsync(m->h_io + 5, m->step + 2, 4, cudaMemcpyDeviceToHost, m->st));
+    CK(cudaStreamSynchronize(m->st));
+    if (m->h_io[4]) {
+        char b[96];
+        snprintf(b, sizeof b, "device error word 0x%x", m->h_io[4]);
+        set_err(b);
+        return false;
+    }
+    return true;
+}
+
+static bool set_step(fwb_model *m, uint32_t tok, size_t pos) {
+    if (pos >= m->kv_ctx) { set_err("transformer_forward: position exceeds KV cache"); return false; }
+    if (tok >= m->cfg.n_vocab) { set_err("transformer_forward: token ID out of range"); return false; }
+    m->h_io[0] = tok;
+    m->h_io[1] = (uint32_t)pos;
+    CK(cudaMemcpyAsync(m->step, m->h_io, 8, cudaMemcpyHostToDevice, m->st));
+    return true;
+}
+
+}  // namespace fwb
+
+// ==========================================================================
+// C ABI
+// ==========================================================================
+using namespace fwb;
+
+extern "C" {
+
+const char *fwb_last_error(void) { return g_err.c_str(); }
+
+int fwb_device_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;
+    return n;
+}
+
+int quant_matvec(const void *weights, size_t weights_size, uint32_t ggml_type, const float *input, float *output,
+                 size_t input_size, size_t output_size) {
+    uint32_t bb, row_bytes;
+    if (!matvec_args_ok(weights, weights_size, ggml_type, input, output, input_size, output_size, bb, row_bytes))
+        return -1;
+    const size_t wbytes = (size_t)output_size * row_bytes;
+    void *dw = nullptr;
+    float *dx = nullptr, *dy = nullptr;
+    int rc = -1;
+    if (cudaMalloc(&dw, wbytes + 64) == cudaSuccess && cudaMalloc(&dx, input_size * 4) == cudaSuccess &&
+        cudaMalloc(&dy, output_size * 4) == cudaSuccess &&
+        cudaMemcpy(dw, weights, wbytes, cudaMemcpyHostToDevice) == cudaSuccess &&
+        cudaMemcpy(dx, input, input_size * 4, cudaMemcpyHostToDevice) == cudaSuccess) {
+        if (matvec_dev(dw, wbytes, ggml_type, dx, dy, input_size, output_size, nullptr) &&
+            cudaMemcpy(output, dy, output_size * 4, cudaMemcpyDeviceToHost) == cudaSuccess)
+            rc = 0;
+        else if (g_err.empty())
+            set_err("quant_matvec: device execution failed");
+    } else {
+        set_err("quant_matvec: device allocation or copy failed");
+    }
+    if (dw) cudaFree(dw);
+    if (dx) cudaFree(dx);
+    if (dy) cudaFree(dy);
+    return rc;
+}
+
+int quant_matvec_dev(const void *d_weights, size_t weights_size, uint32_t ggml_type, const float *d_input,
+                     float *d_output, size_t input_size, size_t output_size, void *stream) {
+    return matvec_dev(d_weights, weights_size, ggml_type, d_input, d_output, input_size, output_size,
+                      static_cast<cudaStream_t>(stream))
+               ? 0
+               : -1;
+}
+
+int quant_dequant_dev(const void *d_weights, size_t weights_size, uint32_t ggml_type, float *d_out, size_t n_values,
+                      void *stream) {
+    uint32_t bb;
+    if (!d_weights || !d_out || !n_values || n_values % 32 || !block_bytes_of(ggml_type, bb) ||
+        weights_size < n_values / 32 * bb) {
+        set_err("quant_dequant_dev: bad arguments");
+        return -1;
+    }
+    const uint64_t n = n_values;
+    const uint32_t grid = (uint32_t)std::min<uint64_t>(4096, (n + 255) / 256);
+    dequant_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<const uint8_t *>(d_weights),
+                                                                         ggml_type, bb, d_out, n);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) { set_err(std::string("dequant launch: ") + cudaGetErrorString(e)); return -1; }
+    return 0;
+}
+
+fwb_model_t *fwb_model_open(const char *path, size_t max_ctx, int device) {
+    g_err.clear();
+    if (!path) { set_err("null path"); return nullptr; }
+    if (cudaSetDevice(device) != cudaSuccess) { set_err("cudaSetDevice failed"); return nullptr; }
+    fwb_model *m = new fwb_model();
+    m->dev = device;
+    m->sms = num_sms(device);
+    const char *ng = getenv("FWB_NO_GRAPH");
+    const char *np = getenv("FWB_NO_PDL");
+    m->use_graph = !(ng && *ng == '1');
+    m->use_pdl = !(np && *np == '1');
+    if (cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking) != cudaSuccess || !set_smem_attrs(device) ||
+        !load_model(m, path, max_ctx) || (m->use_graph && !capture_graph(m))) {
+        std::string e = g_err;
+        free_model(m);
+        set_err(e.empty() ? "model load failed" : e);
+        return nullptr;
+    }
+    return m;
+}
+
+void fwb_model_close(fwb_model_t *m) {
+    if (!m) return;
+    cudaSetDevice(m->dev);
+    free_model(m);
+}
+
+int fwb_model_dims(const fwb_model_t *m, uint32_t *d) {
+    if (!m || !d) return -1;
+    const ModelConfig &c = m->cfg;
+    d[0] = c.n_vocab; d[1] = m->kv_ctx; d[2] = c.n_embd; d[3] = c.n_layer;
+    d[4] = c.n_head; d[5] = c.n_head_kv; d[6] = c.n_ff; d[7] = c.head_dim;
+    return 0;
+}
+
+uint64_t fwb_model_weight_bytes(const fwb_model_t *m) { return m ? m->weight_bytes : 0; }
+
+int fwb_forward(fwb_model_t *m, uint32_t token, size_t pos, float *logits_host) {
+    if (!m) return -1;
+    cudaSetDevice(m->dev);
+    if (!set_step(m, token, pos) || !enqueue_step(m)) return -1;
+    float *dst = logits_host ? logits_host : nullptr;
+    if (dst) {
+        cudaPointerAttributes pa;
+        const bool pinned = cudaPointerGetAttributes(&pa, dst) == cudaSuccess && pa.type == cudaMemoryTypeHost;
+        float *target = pinned ? dst : m->h_logits;
+        if (cudaMemcpyAsync(target, m->logits, (size_t)m->cfg.n_vocab * 4, cudaMemcpyDeviceToHost, m->st) !=
+            cudaSuccess) {
+            set_err("logits copy failed");
+            return -1;
+        }
+        if (!finish(m)) return -1;
+        if (!pinned) std::memcpy(dst, m->h_logits, (size_t)m->cfg.n_vocab * 4);
+        return 0;
+    }
+    return finish(m) ? 0 : -1;
+}
+
+int fwb_forward_argmax(fwb_model_t *m, uint32_t token, size_t pos, uint32_t *next_token) {
+    if (!m) return -1;
+    cudaSetDevice(m->dev);
+    if (!set_step(m, token, pos) || !enqueue_step(m) || !finish(m)) return -1;
+    if (next_token) *next_token = m->h_io[5];
+    return 0;
+}
+
+int fwb_generate_greedy(fwb_model_t *m, uint32_t first, size_t pos0, size_t n, uint32_t *out) {
+    if (!m) return -1;
+    cudaSetDevice(m->dev);
+    if (n == 0) return 0;
+    if (pos0 + n > m->kv_ctx) { set_err("generate: positions exceed KV cache"); return -1; }
+    if (!set_step(m, first, pos0)) return -1;
+    for (size_t i = 0; i < n; ++i)
+        if (!enqueue_step(m)) return -1;
+    if (out && cudaMemcpyAsync(out, m->hist + pos0, n * 4, cudaMemcpyDeviceToHost, m->st) != cudaSuccess) {
+        set_err("token copy failed");
+        return -1;
+    }
+    return finish(m) ? 0 : -1;
+}
+
+static int kv_copy(fwb_model_t *m, size_t layer, size_t pos0, size_t n, float *k, float *v, bool load) {
+    if (!m || !k || !v) return -1;
+    cudaSetDevice(m->dev);
+    const ModelConfig &c = m->cfg;
+    if (layer >= c.n_layer || pos0 > m->kv_ctx || n > m->kv_ctx - pos0) { set_err("kv: range"); return -1; }
+    if (n == 0) return 0;
+    const size_t hd = c.head_dim, KV = c.n_head_kv;
+    const size_t base = layer * KV * m->kv_ctx * hd;
+    for (size_t h = 0; h < KV; ++h) {
+        float *dk = m->kc + base + (h * m->kv_ctx + pos0) * hd;
+        float *dv = m->vc + base + (h * m->kv_ctx + pos0) * hd;
+        cudaError_t e1, e2;
+        if (load) {
+            e1 = cudaMemcpy2DAsync(dk, hd * 4, k + h * hd, KV * hd * 4, hd * 4, n, cudaMemcpyHostToDevice, m->st);
+            e2 = cudaMemcpy2DAsync(dv, hd * 4, v + h * hd, KV * hd * 4, hd * 4, n, cudaMemcpyHostToDevice, m->st);
+        } else {
+            e1 = cudaMemcpy2DAsync(k + h * hd, KV * hd * 4, dk, hd * 4, hd * 4, n, cudaMemcpyDeviceToHost, m->st);
+            e2 = cudaMemcpy2DAsync(v + h * hd, KV * hd * 4, dv, hd * 4, hd * 4, n, cudaMemcpyDeviceToHost, m->st);
+        }
+        if (e1 != cudaSuccess || e2 != cudaSuccess) { set_err("kv copy failed"); return -1; }
+    }
+    if (cudaStreamSynchronize(m->st) != cudaSuccess) { set_err("kv copy failed"); return -1; }
+    return 0;
+}
+
+int fwb_kv_load(fwb_model_t *m, size_t layer, size_t pos0, size_t n, const float *k, const float *v) {
+    return kv_copy(m, layer, pos0, n, const_cast<float *>(k), const_cast<float *>(v), true);
+}
+
+int fwb_kv_read(fwb_model_t *m, size_t layer, size_t pos0, size_t n, float *k, float *v) {
+    return kv_copy(m, layer, pos0, n, k, v, false);
+}
+
+const float *fwb_logits_dev(fwb_model_t *m) { return m ? m->logits : nullptr; }
+void *fwb_stream(fwb_model_t *m) { return m ? (void *)m->st : nullptr; }
+
+}  // extern "C"

@@ -1,0 +1,98 @@
+"""Model shapes: the benchmark spec's configurations plus small test shapes.
+
+Every model is the llama family as forword.c's model_config.c:150-159
+configures it: RMSNorm, gated SiLU FFN, adjacent-pair RoPE, no biases.
+Quant types are GGML type ids: 0 F32, 2 Q4_0, 6 Q5_0, 8 Q8_0.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field, replace
+
+F32, Q4_0, Q5_0, Q8_0 = 0, 2, 6, 8
+TYPE_NAMES = {F32: "F32", Q4_0: "Q4_0", Q5_0: "Q5_0", Q8_0: "Q8_0"}
+BLOCK_BYTES = {Q4_0: 18, Q5_0: 22, Q8_0: 34}
+
+
+@dataclass(frozen=True)
+class ModelShape:
+    name: str
+    n_embd: int
+    n_layer: int
+    n_head: int
+    n_head_kv: int
+    n_ff: int
+    n_vocab: int
+    n_ctx: int
+    rope_base: float = 10000.0
+    eps: float = 1e-5
+    tied: bool = False
+    # ggml type per tensor role
+    t_embd: int = F32
+    t_q: int = Q4_0
+    t_k: int = Q4_0
+    t_v: int = Q4_0
+    t_o: int = Q4_0
+    t_gate: int = Q4_0
+    t_up: int = Q4_0
+    t_down: int = Q4_0
+    t_out: int = Q4_0
+    weight_sd: float = 0.02
+    norm_sd: float = 0.02
+    extra: dict = field(default_factory=dict, compare=False)
+
+    @property
+    def head_dim(self) -> int:
+        return self.n_embd // self.n_head
+
+    def tensor_bytes(self, t: int, rows: int, cols: int) -> int:
+        if t == F32:
+            return rows * cols * 4
+        return rows * cols // 32 * BLOCK_BYTES[t]
+
+    def weight_bytes_per_token(self) -> int:
+        """Algorithmic HBM bytes one decode step must stream: every quantised
+        linear weight once (block bytes incl. scales), fp32 norm weights, and
+        one embedding row."""
+        E, F, hd = self.n_embd, self.n_ff, self.head_dim
+        q = self.n_head * hd
+        kv = self.n_head_kv * hd
+        per_layer = (self.tensor_bytes(self.t_q, q, E) + self.tensor_bytes(self.t_k, kv, E)
+                     + self.tensor_bytes(self.t_v, kv, E) + self.tensor_bytes(self.t_o, E, q)
+                     + self.tensor_bytes(self.t_gate, F, E) + self.tensor_bytes(self.t_up, F, E)
+                     + self.tensor_bytes(self.t_down, E, F) + 2 * E * 4)
+        head_t = self.t_embd if self.tied else self.t_out
+        head = self.tensor_bytes(head_t, self.n_vocab, E)
+        embd_row = self.tensor_bytes(self.t_embd, 1, E)
+        return self.n_layer * per_layer + head + E * 4 + embd_row
+
+    def kv_bytes_per_token(self, n_pos: int) -> int:
+        """fp32 K and V bytes the attention of one decode step reads at n_pos
+        cached positions (all layers)."""
+        return self.n_layer * n_pos * self.n_head_kv * self.head_dim * 4 * 2
+
+
+# --- the benchmark spec's configurations ------------------------------------
+TINY = ModelShape("tiny-q8_0", n_embd=288, n_layer=6, n_head=6, n_head_kv=6, n_ff=768,
+                  n_vocab=32000, n_ctx=256, tied=True, t_embd=Q8_0, t_q=Q8_0, t_k=Q8_0,
+                  t_v=Q8_0, t_o=Q8_0, t_gate=Q8_0, t_up=Q8_0, t_down=Q8_0, t_out=Q8_0)
+
+LLAMA8B_Q4_0 = ModelShape("llama8b-q4_0", n_embd=4096, n_layer=32, n_head=32, n_head_kv=8,
+                          n_ff=14336, n_vocab=128256, n_ctx=8192, rope_base=500000.0)
+
+LLAMA8B_MIXED = ModelShape("llama8b-mixed", n_embd=4096, n_layer=32, n_head=32, n_head_kv=8,
+                           n_ff=14336, n_vocab=128256, n_ctx=8192, rope_base=500000.0,
+                           t_q=Q8_0, t_k=Q8_0, t_v=Q8_0, t_o=Q8_0, t_gate=Q5_0, t_up=Q5_0,
+                           t_down=Q8_0, t_out=Q8_0)
+
+LLAMA70B_Q4_0 = ModelShape("llama70b-q4_0", n_embd=8192, n_layer=80, n_head=64, n_head_kv=8,
+                           n_ff=28672, n_vocab=128256, n_ctx=4096, rope_base=500000.0)
+
+# --- small shapes for parity tests ----------------------------------------------
+SMALL_Q4_0 = ModelShape("small-q4_0", n_embd=512, n_layer=2, n_head=4, n_head_kv=2, n_ff=1024,
+                        n_vocab=2048, n_ctx=512, rope_base=500000.0)
+SMALL_MIXED = replace(SMALL_Q4_0, name="small-mixed", t_q=Q8_0, t_k=Q8_0, t_v=Q8_0, t_o=Q8_0,
+                      t_gate=Q5_0, t_up=Q5_0, t_down=Q8_0, t_out=Q8_0)
+SMALL_TIED_Q8 = replace(TINY, name="small-tied-q8_0", n_layer=2, n_vocab=1000, n_ctx=128)
+
+CONFIGS = {c.name: c for c in (TINY, LLAMA8B_Q4_0, LLAMA8B_MIXED, LLAMA70B_Q4_0,
+                               SMALL_Q4_0, SMALL_MIXED, SMALL_TIED_Q8)}

@@ -1,0 +1,135 @@
+/*
+ * forword_b200.h — C ABI of libforword_b200.so, the B200 (sm_100a) decode
+ * path of forword.c.
+ *
+ * Plain C types only (pointers, sizes, ints).  Every function returns 0 on
+ * success and -1 on failure (NULL for constructors), matching the reference's
+ * error convention (transformer.c:156-164, quant_matvec.c:270-289); the
+ * failure text is available from fwb_last_error().
+ *
+ * Threading: like the reference (single-threaded, non-reentrant), one model
+ * handle must be used from one thread at a time.  Each model owns one CUDA
+ * stream on its device.
+ *
+ * The drop-in entry points with the reference's own names
+ * (transformer_init / transformer_forward / transformer_free) are in
+ * forword.c_b200/shim/transformer_b200.c, which a maintainer compiles
+ * together with forword.c's unchanged host C (gguf.c, model_config.c,
+ * tokenizer.c, ...); it calls the fwb_* functions below.
+ */
+#ifndef FORWORD_B200_H
+#define FORWORD_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Text of the last error on this thread ("" if none).  Never NULL. */
+const char *fwb_last_error(void);
+
+/* Number of visible CUDA devices (0 when none). */
+int fwb_device_count(void);
+
+/* ------------------------------------------------------------------------
+ * Quantised matrix-vector product.
+ * ------------------------------------------------------------------------ */
+
+/*
+ * Replaces quant_matvec (quant_matvec.h:7-15, quant_matvec.c:263-312) with
+ * the same signature and argument meaning: `weights` holds output_size rows
+ * of GGUF blocks (row r at r * (input_size/32) * block_bytes), input[in] and
+ * output[out] are host fp32 arrays.  The call copies weights and input to the
+ * current device, runs the GEMV there and copies output back.
+ * Types: 2 (Q4_0), 6 (Q5_0), 8 (Q8_0).  The reference instead supports
+ * 6, 7 (Q5_1), 8, 12 (Q4_K), 14 (Q6_K) and lacks Q4_0.
+ * Returns -1 for NULL pointers, zero sizes, an unsupported type,
+ * input_size % 32 != 0 or weights_size < output_size * row bytes, like the
+ * reference.
+ */
+int quant_matvec(const void *weights, size_t weights_size, uint32_t ggml_type,
+                 const float *input, float *output, size_t input_size,
+                 size_t output_size);
+
+/*
+ * Device-pointer form of quant_matvec for callers whose data already lives
+ * in HBM.  d_weights must lie inside a cudaMalloc allocation and be 2-byte
+ * aligned (the kernel reads up to 15 bytes either side of the rows, rounding
+ * to 16-byte copies); d_input / d_output are fp32 device arrays.  `stream`
+ * is a cudaStream_t (NULL = legacy default stream).  Asynchronous: returns
+ * after enqueueing.
+ */
+int quant_matvec_dev(const void *d_weights, size_t weights_size, uint32_t ggml_type,
+                     const float *d_input, float *d_output, size_t input_size,
+                     size_t output_size, void *stream);
+
+/*
+ * Dequantise n_values (a multiple of 32) from Q4_0 / Q5_0 / Q8_0 blocks into
+ * fp32 on the device, bit-identical to the reference decoders (q8_0_decode
+ * quant.c:232-263, q5_0_decode linear.c:40-56, and GGML's Q4_0).
+ */
+int quant_dequant_dev(const void *d_weights, size_t weights_size, uint32_t ggml_type,
+                      float *d_out, size_t n_values, void *stream);
+
+/* ------------------------------------------------------------------------
+ * Decode model (transformer.h:39-48 semantics).
+ * ------------------------------------------------------------------------ */
+
+typedef struct fwb_model fwb_model_t;
+
+/*
+ * transformer_init (transformer.c:14-147): open a GGUF file, derive the
+ * model configuration, clamp the KV length (max_ctx 0 -> min(n_ctx, 4096);
+ * max_ctx > n_ctx -> n_ctx) and upload every tensor once to HBM in its GGUF
+ * byte layout.  `device` selects the CUDA device.  NULL on failure.
+ */
+fwb_model_t *fwb_model_open(const char *gguf_path, size_t max_ctx, int device);
+
+/* transformer_free (transformer.c:149-165).  NULL is accepted. */
+void fwb_model_close(fwb_model_t *m);
+
+/* dims[8] = n_vocab, kv_ctx, n_embd, n_layer, n_head, n_head_kv, n_ff, head_dim */
+int fwb_model_dims(const fwb_model_t *m, uint32_t *dims);
+
+/* Quantised bytes one decode step streams (weights + norms + one embedding row). */
+uint64_t fwb_model_weight_bytes(const fwb_model_t *m);
+
+/*
+ * transformer_forward (transformer.c:149-326): feed token_id at position pos
+ * and write n_vocab fp32 logits to logits_host (host memory; may be NULL to
+ * skip the copy).  Errors as the reference: pos >= kv_ctx or
+ * token_id >= n_vocab -> -1.
+ */
+int fwb_forward(fwb_model_t *m, uint32_t token_id, size_t pos, float *logits_host);
+
+/* Same step, returning only the greedy next token (sampler_argmax,
+ * sampler.c:28-32: the lowest index among equal maxima). */
+int fwb_forward_argmax(fwb_model_t *m, uint32_t token_id, size_t pos, uint32_t *next_token);
+
+/*
+ * Greedy decode of n_steps tokens entirely on the device: step i feeds the
+ * token chosen by step i-1 (first_token for i = 0) at position pos0 + i.
+ * tokens_out[i] receives the token chosen by step i.
+ */
+int fwb_generate_greedy(fwb_model_t *m, uint32_t first_token, size_t pos0, size_t n_steps,
+                        uint32_t *tokens_out);
+
+/*
+ * Write (load) or read K/V of n positions [pos0, pos0+n) of one layer.
+ * k and v are host fp32 arrays [n][n_head_kv][head_dim] — the reference's
+ * kv_cache row order (kv_cache.h:13,45-51).
+ */
+int fwb_kv_load(fwb_model_t *m, size_t layer, size_t pos0, size_t n, const float *k,
+                const float *v);
+int fwb_kv_read(fwb_model_t *m, size_t layer, size_t pos0, size_t n, float *k, float *v);
+
+/* Device logits of the last step (n_vocab fp32) and the model's CUDA stream. */
+const float *fwb_logits_dev(fwb_model_t *m);
+void *fwb_stream(fwb_model_t *m);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FORWORD_B200_H */
