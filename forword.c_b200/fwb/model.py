@@ -1,0 +1,116 @@
+"""Python handle over the C ABI of libforword_b200.so (include/forword_b200.h).
+
+Thin ctypes plumbing only: every call goes to the CUDA library; a missing
+library raises (no CPU fallback).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import native
+
+
+class FwbError(RuntimeError):
+    pass
+
+
+def _err(lib) -> str:
+    return lib.fwb_last_error().decode(errors="replace")
+
+
+class Model:
+    """One decode model on one GPU (transformer_t of forword.c)."""
+
+    def __init__(self, path: str, max_ctx: int = 0, device: int = 0):
+        self.lib = native.product()
+        self.h = self.lib.fwb_model_open(path.encode(), max_ctx, device)
+        if not self.h:
+            raise FwbError(f"fwb_model_open({path}): {_err(self.lib)}")
+        d = (ctypes.c_uint32 * 8)()
+        self.lib.fwb_model_dims(self.h, d)
+        (self.n_vocab, self.kv_ctx, self.n_embd, self.n_layer, self.n_head, self.n_head_kv,
+         self.n_ff, self.head_dim) = list(d)
+        self._logits = np.zeros(self.n_vocab, dtype=np.float32)
+
+    def close(self) -> None:
+        if self.h:
+            self.lib.fwb_model_close(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def weight_bytes(self) -> int:
+        return int(self.lib.fwb_model_weight_bytes(self.h))
+
+    @property
+    def stream(self) -> int:
+        return int(self.lib.fwb_stream(self.h) or 0)
+
+    def forward(self, token: int, pos: int, out: np.ndarray | None = None) -> np.ndarray:
+        """transformer_forward: returns (a copy of) the n_vocab logits."""
+        dst = self._logits if out is None else out
+        rc = self.lib.fwb_forward(self.h, token, pos,
+                                  dst.ctypes.data_as(ctypes.POINTER(ctypes.c_float)))
+        if rc != 0:
+            raise FwbError(f"fwb_forward: {_err(self.lib)}")
+        return dst.copy() if out is None else dst
+
+    def try_forward(self, token: int, pos: int) -> int:
+        """Raw return code of fwb_forward (0 / -1) for error-path tests."""
+        return int(self.lib.fwb_forward(self.h, token, pos, None))
+
+    def forward_argmax(self, token: int, pos: int) -> int:
+        nxt = ctypes.c_uint32()
+        if self.lib.fwb_forward_argmax(self.h, token, pos, ctypes.byref(nxt)) != 0:
+            raise FwbError(f"fwb_forward_argmax: {_err(self.lib)}")
+        return int(nxt.value)
+
+    def generate_greedy(self, first: int, pos0: int, n: int) -> np.ndarray:
+        out = np.zeros(n, dtype=np.uint32)
+        rc = self.lib.fwb_generate_greedy(self.h, first, pos0, n,
+                                          out.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)))
+        if rc != 0:
+            raise FwbError(f"fwb_generate_greedy: {_err(self.lib)}")
+        return out
+
+    def kv_load(self, layer: int, pos0: int, k: np.ndarray, v: np.ndarray) -> None:
+        k = np.ascontiguousarray(k, dtype=np.float32)
+        v = np.ascontiguousarray(v, dtype=np.float32)
+        n = k.shape[0]
+        fp = ctypes.POINTER(ctypes.c_float)
+        if self.lib.fwb_kv_load(self.h, layer, pos0, n, k.ctypes.data_as(fp), v.ctypes.data_as(fp)) != 0:
+            raise FwbError(f"fwb_kv_load: {_err(self.lib)}")
+
+    def kv_read(self, layer: int, pos0: int, n: int) -> tuple[np.ndarray, np.ndarray]:
+        k = np.zeros((n, self.n_head_kv, self.head_dim), dtype=np.float32)
+        v = np.zeros_like(k)
+        fp = ctypes.POINTER(ctypes.c_float)
+        if self.lib.fwb_kv_read(self.h, layer, pos0, n, k.ctypes.data_as(fp), v.ctypes.data_as(fp)) != 0:
+            raise FwbError(f"fwb_kv_read: {_err(self.lib)}")
+        return k, v
+
+
+def quant_matvec(w: np.ndarray, ggml_type: int, x: np.ndarray, n_out: int) -> np.ndarray:
+    """quant_matvec with host buffers (the reference's signature)."""
+    lib = native.product()
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.zeros(n_out, dtype=np.float32)
+    fp = ctypes.POINTER(ctypes.c_float)
+    rc = lib.quant_matvec(w.ctypes.data, w.nbytes, ggml_type, x.ctypes.data_as(fp),
+                          y.ctypes.data_as(fp), x.size, n_out)
+    if rc != 0:
+        raise FwbError(f"quant_matvec: {_err(lib)}")
+    return y

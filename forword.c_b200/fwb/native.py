@@ -50,7 +50,7 @@ def product():
         if not os.path.exists(PRODUCT_SO):
             raise RuntimeError(f"{PRODUCT_SO} is missing: build it with "
                                f"`make -C {PKG_DIR}` (there is no CPU fallback)")
-        lib = _c.CDLL(PRODUCT_SO, mode=_c.RTLD_GLOBAL)
+        lib = _c.CDLL(PRODUCT_SO)
         _declare(lib)
         _product = lib
     return _product

@@ -1,0 +1,117 @@
+"""Generate the committed golden fixtures of tests/golden/.
+
+Run in a container that has the reference sources (for oracle/_ref) and the
+gguf-py package:  python tests/golden/make_golden.py
+
+quant_gguf_py.npz
+    Q4_0 / Q5_0 / Q8_0 blocks quantised by gguf-py (llama.cpp's gguf-py
+    0.19.0, gguf.quants.quantize) from seeded normals, plus hand-made blocks
+    with special fp16 scales (subnormal, negative, zero, large), and gguf-py's
+    own dequantisation of every block.  Pins the Q4_0 restatement (the
+    reference has no Q4_0 decoder) and the Q5_0 / Q8_0 decoders against an
+    independent implementation of the GGML formats.
+
+ref_decode_<model>.npz
+    The compiled reference's own transformer_forward (oracle/_ref) on seeded
+    synthetic GGUFs: the sha256 of the model bytes, the greedy token stream
+    and the logits of every step.  For Q4_0 the reference runs with the
+    patch-free Q4_0 add-on of oracle/ref_q4_0_addon.c.  The `kvprefill`
+    variant first writes fp16-rounded N(0,1) K/V into positions [0, 96)
+    through the reference's kv_k / kv_v.
+"""
+from __future__ import annotations
+
+import hashlib
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, os.path.join(ROOT, "forword.c_b200"))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+from fwb import configs, gguf_synth  # noqa: E402
+
+GOLDEN_MODELS = {
+    "tied_q8_0": (configs.SMALL_TIED_Q8, 11),
+    "mixed": (configs.SMALL_MIXED, 12),
+    "q4_0": (configs.SMALL_Q4_0, 13),
+}
+STEPS = 24
+FIRST_TOKEN = 7
+PREFILL = 96
+
+
+def sha256(path: str) -> str:
+    h = hashlib.sha256()
+    with open(path, "rb") as f:
+        for chunk in iter(lambda: f.read(1 << 20), b""):
+            h.update(chunk)
+    return h.hexdigest()
+
+
+def prefill_kv(cfg, layer: int, n: int, seed: int):
+    rng = np.random.default_rng(seed * 1000 + layer)
+    shape = (n, cfg.n_head_kv, cfg.head_dim)
+    k = rng.standard_normal(shape).astype(np.float16).astype(np.float32)
+    v = rng.standard_normal(shape).astype(np.float16).astype(np.float32)
+    return k, v
+
+
+def make_quant():
+    import gguf
+    from gguf import quants
+    rng = np.random.default_rng(2024)
+    out = {}
+    for name, t in (("q4_0", gguf.GGMLQuantizationType.Q4_0),
+                    ("q5_0", gguf.GGMLQuantizationType.Q5_0),
+                    ("q8_0", gguf.GGMLQuantizationType.Q8_0)):
+        x = (rng.standard_normal((64, 256)) * rng.uniform(1e-4, 10.0, (64, 1))).astype(np.float32)
+        q = np.ascontiguousarray(quants.quantize(x, t)).reshape(-1)
+        bb = {"q4_0": 18, "q5_0": 22, "q8_0": 34}[name]
+        blocks = q.reshape(-1, bb).copy()
+        # special fp16 scales: subnormal, negative, zero, large, max normal
+        for i, d in enumerate((0x0001, 0x03FF, 0xBC00, 0x0000, 0x7BFF, 0x3C00)):
+            blocks[i, 0] = d & 0xFF
+            blocks[i, 1] = d >> 8
+        raw = blocks.reshape(-1)
+        deq = quants.dequantize(raw.reshape(1, -1), t).reshape(-1).astype(np.float32)
+        out[name + "_bytes"] = raw
+        out[name + "_deq"] = deq
+    np.savez_compressed(os.path.join(HERE, "quant_gguf_py.npz"), **out)
+
+
+def make_decode(tmp: str):
+    import pyoracle
+    for tag, (cfg, seed) in GOLDEN_MODELS.items():
+        path = gguf_synth.write_model(os.path.join(tmp, f"{tag}.gguf"), cfg, seed=seed)
+        for variant in ("plain", "kvprefill"):
+            ref = pyoracle.RefModel(path, 0)
+            pos0 = 0
+            if variant == "kvprefill":
+                for layer in range(cfg.n_layer):
+                    k, v = prefill_kv(cfg, layer, PREFILL, seed)
+                    ref.kv_load(layer, 0, k, v)
+                pos0 = PREFILL
+            tok = FIRST_TOKEN
+            toks, logits = [], []
+            for i in range(STEPS):
+                lg = ref.forward(tok, pos0 + i)
+                logits.append(lg)
+                tok = int(np.argmax(lg))
+                toks.append(tok)
+            ref.close()
+            np.savez_compressed(os.path.join(HERE, f"ref_decode_{tag}_{variant}.npz"),
+                                sha256=np.array(sha256(path)), seed=np.array(seed),
+                                first=np.array(FIRST_TOKEN), pos0=np.array(pos0),
+                                tokens=np.array(toks, np.uint32), logits=np.stack(logits))
+
+
+if __name__ == "__main__":
+    import tempfile
+    make_quant()
+    with tempfile.TemporaryDirectory() as tmp:
+        make_decode(tmp)
+    print("golden fixtures written to", HERE)
