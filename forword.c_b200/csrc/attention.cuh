@@ -9,8 +9,8 @@
 // slice of positions of KV head h and serves all GQ = n_head/n_kv query
 // heads of that group, so each K/V row is read from HBM once per step.  The
 // KV cache layout is [kv_head][ctx][head_dim] fp32, so a slice is one
-// contiguous range.  Each warp runs an online softmax over tiles of
-// min(8, 32/GQ) positions: lanes own 4 dims, the (position, head) partial
+// contiguous range.  Each warp runs an online softmax over tiles of 16/GQ
+// positions (8 when GQ = 1): lanes own 4 dims, the (position, head) partial
 // dots of a tile are finished with one butterfly reduce-scatter.  Warps are merged in shared memory, each CTA writes one
 // (max, sum, o[]) partial per query head, and the last CTA of a KV head to
 // finish (atomic ticket) merges the n_split partials and writes the output.
@@ -25,43 +25,58 @@ struct AttnArgs {
     float *out;            // [n_head][HD]
     float *part;           // scratch [n_kv][n_split][GQ][HD + 2]
     uint32_t *ticket;      // [n_kv], zero between launches
-    uint32_t kv_ctx, n_split;
+    uint32_t kv_ctx, n_split, n_kv;
     float scale;           // 1/sqrtf(head_dim), attention.c:143
     const uint32_t *step;  // [1] = pos
     uint32_t *err;
 };
 
-constexpr int kAttnWarps = 4;
+constexpr int kAttnWarps = 4;          // warps per CTA of the standalone kernel
+constexpr uint32_t kMinSplitPos = 256;  // positions per split at least
+constexpr uint32_t kMaxSplits = 64;
 
-template <int HD, int GQ>
-__global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const __grid_constant__ AttnArgs a) {
+// Splits in use at n_pos positions (short contexts merge few partials).
+__device__ __forceinline__ uint32_t attn_splits_in_use(const AttnArgs &a, uint32_t n_pos) {
+    return min(a.n_split, (n_pos + kMinSplitPos - 1) / kMinSplitPos);
+}
+
+// Shared scratch of one attention item for NW warps.
+template <int HD, int GQ, int NW>
+struct AttnSmem {
+    float pbuf[NW][32];
+    float wm[NW][GQ], wl[NW][GQ];
+    float wo[NW][GQ][HD];
+    float sw[kMaxSplits][GQ];
+    float sL[GQ];
+    uint32_t last_flag;
+};
+
+// One work item: KV head h, split sp of n_use.  All NW warps of the CTA take
+// part.  K/V, q and the partials are read with L2-only loads (other CTAs of
+// the persistent kernel wrote them in this very step).
+template <int HD, int GQ, int NW>
+__device__ void attn_item(const AttnArgs &a, uint32_t h, uint32_t sp, uint32_t n_pos, uint32_t n_use,
+                          AttnSmem<HD, GQ, NW> &sh) {
     static_assert(HD % 4 == 0 && HD <= 128, "head_dim");
     static_assert(GQ == 1 || GQ == 2 || GQ == 4 || GQ == 8, "group");
-    constexpr int TILE = (32 / GQ) < 8 ? (32 / GQ) : 8;  // positions per tile
-    constexpr int NVAL = TILE * GQ;                       // partial dots per tile (8..32)
+    // positions per tile: 16 (position, head) dots per tile for GQ >= 2
+    // (8 for GQ = 1), keeping the K/V tile in registers within the budget
+    constexpr int TILE = GQ == 1 ? 8 : 16 / GQ;
+    constexpr int NVAL = TILE * GQ;                       // partial dots per tile (8 or 16)
     constexpr int REP = 32 / NVAL;                        // lanes holding each finished value
     constexpr int LA = HD / 4;                            // active lanes
-    __shared__ float pbuf[kAttnWarps][32];
-    __shared__ float wm[kAttnWarps][GQ], wl[kAttnWarps][GQ];
-    __shared__ float wo[kAttnWarps][GQ][HD];
-    __shared__ uint32_t last_flag;
-
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const uint32_t h = blockIdx.x, sp = blockIdx.y;
-    pdl_launch();
-    pdl_wait();
 
-    const uint32_t n_pos = a.step[1] + 1;
-    const uint32_t chunk = (n_pos + a.n_split - 1) / a.n_split;
+    const uint32_t chunk = (n_pos + n_use - 1) / n_use;
     const uint32_t c0 = min(n_pos, sp * chunk), c1 = min(n_pos, c0 + chunk);
-    const uint32_t wchunk = (c1 - c0 + kAttnWarps - 1) / kAttnWarps;
+    const uint32_t wchunk = (c1 - c0 + NW - 1) / NW;
     const uint32_t w0 = min(c1, c0 + warp * wchunk), w1 = min(c1, w0 + wchunk);
 
     const bool lact = lane < LA;
     float qv[GQ][4], o[GQ][4], m[GQ], l[GQ];
 #pragma unroll
     for (int g = 0; g < GQ; ++g) {
-        const float4 t = lact ? *reinterpret_cast<const float4 *>(a.q + (size_t)(h * GQ + g) * HD + 4 * lane)
+        const float4 t = lact ? __ldcg(reinterpret_cast<const float4 *>(a.q + (size_t)(h * GQ + g) * HD + 4 * lane))
                               : make_float4(0.f, 0.f, 0.f, 0.f);
         qv[g][0] = t.x; qv[g][1] = t.y; qv[g][2] = t.z; qv[g][3] = t.w;
         m[g] = -INFINITY;
@@ -77,8 +92,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const __gr
 #pragma unroll
         for (int p = 0; p < TILE; ++p) {
             const bool ok = lact && t0 + p < w1;
-            kt[p] = ok ? *reinterpret_cast<const float4 *>(kb + (size_t)(t0 + p) * HD) : make_float4(0.f, 0.f, 0.f, 0.f);
-            vt[p] = ok ? *reinterpret_cast<const float4 *>(vb + (size_t)(t0 + p) * HD) : make_float4(0.f, 0.f, 0.f, 0.f);
+            kt[p] = ok ? __ldcg(reinterpret_cast<const float4 *>(kb + (size_t)(t0 + p) * HD)) : make_float4(0.f, 0.f, 0.f, 0.f);
+            vt[p] = ok ? __ldcg(reinterpret_cast<const float4 *>(vb + (size_t)(t0 + p) * HD)) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
         float v[NVAL];
 #pragma unroll
@@ -120,7 +135,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const __gr
 #pragma unroll
         for (int o_ = 32 / TILE; o_ < 32; o_ <<= 1) ts += __shfl_xor_sync(0xffffffffu, ts, o_);
         const float alpha = expf(mg - mn);
-        pbuf[warp][vi] = pe;  // the REP lanes of a value write the same number
+        sh.pbuf[warp][vi] = pe;  // the REP lanes of a value write the same number
 #pragma unroll
         for (int g = 0; g < GQ; ++g) {
             const float al = __shfl_sync(0xffffffffu, alpha, g * REP);
@@ -136,7 +151,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const __gr
         for (int p = 0; p < TILE; ++p)
 #pragma unroll
             for (int g = 0; g < GQ; ++g) {
-                const float w = pbuf[warp][p * GQ + g];
+                const float w = sh.pbuf[warp][p * GQ + g];
                 o[g][0] = fmaf(w, vt[p].x, o[g][0]);
                 o[g][1] = fmaf(w, vt[p].y, o[g][1]);
                 o[g][2] = fmaf(w, vt[p].z, o[g][2]);
@@ -148,47 +163,88 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const __gr
     // merge the warps of this CTA
 #pragma unroll
     for (int g = 0; g < GQ; ++g) {
-        if (lane == 0) { wm[warp][g] = m[g]; wl[warp][g] = l[g]; }
+        if (lane == 0) { sh.wm[warp][g] = m[g]; sh.wl[warp][g] = l[g]; }
         if (lact)
 #pragma unroll
-            for (int d = 0; d < 4; ++d) wo[warp][g][4 * lane + d] = o[g][d];
+            for (int d = 0; d < 4; ++d) sh.wo[warp][g][4 * lane + d] = o[g][d];
     }
     __syncthreads();
+    if (n_use == 1) {  // the only split: normalise and write the output directly
+        for (uint32_t i = tid; i < (uint32_t)(GQ * HD); i += blockDim.x) {
+            const uint32_t g = i / HD, d = i % HD;
+            float M = sh.wm[0][g];
+            for (int w = 1; w < NW; ++w) M = fmaxf(M, sh.wm[w][g]);
+            float L = 0.f, O = 0.f;
+            for (int w = 0; w < NW; ++w) {
+                const float f = sh.wm[w][g] == -INFINITY ? 0.f : expf(sh.wm[w][g] - M);
+                L = fmaf(sh.wl[w][g], f, L);
+                O = fmaf(sh.wo[w][g][d], f, O);
+            }
+            a.out[(size_t)(h * GQ + g) * HD + d] = __fdiv_rn(O, L);
+        }
+        __syncthreads();
+        return;
+    }
     float *pp = a.part + ((size_t)h * a.n_split + sp) * GQ * (HD + 2);
     for (uint32_t i = tid; i < (uint32_t)(GQ * HD); i += blockDim.x) {
         const uint32_t g = i / HD, d = i % HD;
-        float M = wm[0][g];
-        for (int w = 1; w < kAttnWarps; ++w) M = fmaxf(M, wm[w][g]);
+        float M = sh.wm[0][g];
+        for (int w = 1; w < NW; ++w) M = fmaxf(M, sh.wm[w][g]);
         float L = 0.f, O = 0.f;
-        for (int w = 0; w < kAttnWarps; ++w) {
-            const float f = wm[w][g] == -INFINITY ? 0.f : expf(wm[w][g] - M);
-            L = fmaf(wl[w][g], f, L);
-            O = fmaf(wo[w][g][d], f, O);
+        for (int w = 0; w < NW; ++w) {
+            const float f = sh.wm[w][g] == -INFINITY ? 0.f : expf(sh.wm[w][g] - M);
+            L = fmaf(sh.wl[w][g], f, L);
+            O = fmaf(sh.wo[w][g][d], f, O);
         }
         pp[g * (HD + 2) + 2 + d] = O;
         if (d == 0) { pp[g * (HD + 2)] = M; pp[g * (HD + 2) + 1] = L; }
     }
     __threadfence();
     __syncthreads();
-    if (tid == 0) last_flag = (atomicAdd(&a.ticket[h], 1u) == a.n_split - 1) ? 1u : 0u;
+    if (tid == 0) sh.last_flag = (atomicAdd(&a.ticket[h], 1u) == n_use - 1) ? 1u : 0u;
     __syncthreads();
-    if (!last_flag) return;
-    __threadfence();
-    const volatile float *P = a.part + (size_t)h * a.n_split * GQ * (HD + 2);
-    for (uint32_t i = tid; i < (uint32_t)(GQ * HD); i += blockDim.x) {
-        const uint32_t g = i / HD, d = i % HD;
-        float M = -INFINITY;
-        for (uint32_t s = 0; s < a.n_split; ++s) M = fmaxf(M, P[(s * GQ + g) * (HD + 2)]);
-        float L = 0.f, O = 0.f;
-        for (uint32_t s = 0; s < a.n_split; ++s) {
-            const float ms = P[(s * GQ + g) * (HD + 2)];
-            const float f = ms == -INFINITY ? 0.f : expf(ms - M);
-            L = fmaf(P[(s * GQ + g) * (HD + 2) + 1], f, L);
-            O = fmaf(P[(s * GQ + g) * (HD + 2) + 2 + d], f, O);
+    if (sh.last_flag) {
+        __threadfence();
+        // merge the n_use partials of this KV head: first the per-split weights
+        // exp(m_s - M) (one load per (split, head)), then every output element
+        // sums its split values with independent L2 loads
+        const float *P = a.part + (size_t)h * a.n_split * GQ * (HD + 2);
+        for (uint32_t i = tid; i < n_use * GQ; i += blockDim.x) sh.sw[i / GQ][i % GQ] = __ldcg(P + (size_t)i * (HD + 2));
+        __syncthreads();
+        if (tid < (uint32_t)GQ) {
+            float M = -INFINITY;
+            for (uint32_t s = 0; s < n_use; ++s) M = fmaxf(M, sh.sw[s][tid]);
+            float L = 0.f;
+            for (uint32_t s = 0; s < n_use; ++s) {
+                const float f = sh.sw[s][tid] == -INFINITY ? 0.f : expf(sh.sw[s][tid] - M);
+                L = fmaf(__ldcg(P + ((size_t)s * GQ + tid) * (HD + 2) + 1), f, L);
+                sh.sw[s][tid] = f;
+            }
+            sh.sL[tid] = L;
         }
-        a.out[(size_t)(h * GQ + g) * HD + d] = __fdiv_rn(O, L);
+        __syncthreads();
+        for (uint32_t i = tid; i < (uint32_t)(GQ * HD); i += blockDim.x) {
+            const uint32_t g = i / HD, d = i % HD;
+            float O = 0.f;
+#pragma unroll 8
+            for (uint32_t s = 0; s < n_use; ++s) O = fmaf(__ldcg(P + ((size_t)s * GQ + g) * (HD + 2) + 2 + d), sh.sw[s][g], O);
+            a.out[(size_t)(h * GQ + g) * HD + d] = __fdiv_rn(O, sh.sL[g]);
+        }
+        if (tid == 0) a.ticket[h] = 0;
     }
-    if (tid == 0) a.ticket[h] = 0;
+    __syncthreads();  // the scratch may be reused by the next item
+}
+
+// Standalone kernel: grid (n_kv, n_split), one item per CTA.
+template <int HD, int GQ>
+__global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const __grid_constant__ AttnArgs a) {
+    __shared__ AttnSmem<HD, GQ, kAttnWarps> sh;
+    pdl_launch();
+    pdl_wait();
+    const uint32_t n_pos = a.step[1] + 1;
+    const uint32_t n_use = attn_splits_in_use(a, n_pos);
+    if (blockIdx.y >= n_use) return;
+    attn_item<HD, GQ, kAttnWarps>(a, blockIdx.x, blockIdx.y, n_pos, n_use, sh);
 }
 
 }  // namespace fwb

@@ -21,6 +21,7 @@ enum : uint32_t {
     ERR_BAD_POS = 1u << 3,      // step position outside the KV cache
     ERR_BAD_TOKEN = 1u << 4,    // token id outside the vocabulary
     ERR_ATTN_TIMEOUT = 1u << 5,
+    ERR_GRID_SYNC = 1u << 6,     // a grid barrier of the persistent kernel timed out
 };
 
 // Upper bound on polls of one barrier phase.  With the back-off below this is
@@ -87,6 +88,22 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         "[%3];" ::"r"(smem_u32(dst)),
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
+}
+
+// Bulk prefetch of [src, src+bytes) into L2 (no shared memory, no
+// completion tracking).  src 16-byte aligned, bytes % 16 == 0.
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// gpu-scope release add / acquire load (grid barrier)
+__device__ __forceinline__ void red_release_add(uint32_t *p, uint32_t v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
 }
 
 // Programmatic dependent launch.  wait: block until the preceding kernel in

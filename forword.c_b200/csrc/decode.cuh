@@ -1,0 +1,284 @@
+// decode.cuh — the persistent decode-step kernel.
+//
+// One launch runs a whole transformer_forward (transformer.c:149-326) for
+// one token: embedding, then per layer QKV+RoPE+KV-append, attention,
+// o-proj+residual, gate/up+SwiGLU, down+residual, and the LM head with the
+// greedy argmax.  Grid = one CTA per SM (cooperative launch, so every CTA is
+// resident); phases are separated by a grid barrier.
+//
+// The weight ring is shared by all GEMV phases.  Each CTA's weights for the
+// whole step form one sequence of ring stages (global stage index j); when
+// the last warp finishes stage j it immediately issues stage j + NS, even if
+// that stage belongs to a later phase.  So weight streaming does not stop at
+// phase boundaries: while the CTA waits at a barrier or runs the attention
+// phase, the next GEMV's first NS stages are already landing in shared
+// memory.
+#pragma once
+#include "attention.cuh"
+#include "gemv.cuh"
+#include "misc_kernels.cuh"
+
+namespace fwb {
+
+struct EmbedArgs {
+    const uint8_t *table;
+    uint32_t type, cols;
+    uint64_t row_bytes;
+    const uint32_t *step;
+    float *x;
+};
+
+enum PhaseKind : uint32_t { PH_EMBED = 0, PH_GEMV = 1, PH_ATTN = 2 };
+
+struct Phase {
+    uint32_t kind, qt, mode, a4;  // PH_GEMV: quant type, mode, 4-byte-aligned units
+    uint32_t hd, gq;              // PH_ATTN: head_dim, GQA group
+    GemvArgs g;
+    AttnArgs at;
+    EmbedArgs e;
+};
+
+// This CTA's weight stream of one GEMV phase (host-computed).
+struct StageSrc {
+    uint64_t a, b;         // first source byte of the CTA's rows (gate / up for SWIGLU; b = 0 otherwise)
+    uint32_t rows;         // rows of matrix a (= pairs for SWIGLU)
+    uint32_t row_bytes;
+    uint32_t R;            // local rows per stage (both halves for SWIGLU)
+    uint32_t first;        // global index of the phase's first stage in this CTA's ring sequence
+    uint32_t n_st;         // stages (0 for phases without weights)
+    uint32_t paired;
+};
+
+constexpr uint32_t kDecodeThreads = 512;
+
+struct DecodeArgs {
+    const Phase *ph;
+    const StageSrc *src;   // [gridDim.x][n_ph]
+    uint32_t n_ph;
+    uint32_t total_st;     // stages per CTA (max over CTAs is fine: CTAs read their own table)
+    uint32_t NS, stage_bytes, scratch_bytes;
+    uint32_t *sync;        // [0] barrier arrivals (zeroed before each launch), [1] abort
+    uint32_t *err;
+    uint32_t *n_st_cta;    // [gridDim.x] stages of each CTA
+    unsigned long long *trace;  // optional: CTA 0's globaltimer at phase start [2p] and barrier arrival [2p+1]
+};
+
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Issue stage k of one CTA stream into ring slot `slot` (one thread), or,
+// with slot == kPrefetchOnly, only prefetch its bytes into L2.
+constexpr uint32_t kPrefetchOnly = 0xffffffffu;
+
+__device__ __forceinline__ void issue_src(const StageSrc &s, uint32_t k, uint8_t *ring, uint32_t stage_bytes,
+                                          uint64_t *full, uint32_t slot) {
+    const bool pf = slot == kPrefetchOnly;
+    uint8_t *dst = pf ? nullptr : ring + (size_t)slot * stage_bytes;
+    if (!s.paired) {
+        const uint32_t r0 = k * s.R, nr = min(s.R, s.rows - r0);
+        const uint64_t src = s.a + (uint64_t)r0 * s.row_bytes;
+        const uint64_t s0 = src & ~15ull;
+        const uint32_t bytes = (uint32_t)(((src + (uint64_t)nr * s.row_bytes + 15) & ~15ull) - s0);
+        if (pf) { bulk_prefetch_l2(reinterpret_cast<const void *>(s0), bytes); return; }
+        mbar_arrive_expect_tx(&full[slot], bytes);
+        bulk_g2s(dst, reinterpret_cast<const void *>(s0), bytes, &full[slot]);
+    } else {
+        const uint32_t p0 = k * (s.R / 2), np = min(s.R / 2, s.rows - p0);
+        const uint64_t g = s.a + (uint64_t)p0 * s.row_bytes, u = s.b + (uint64_t)p0 * s.row_bytes;
+        const uint64_t g0 = g & ~15ull, u0 = u & ~15ull;
+        const uint32_t gb = (uint32_t)(((g + (uint64_t)np * s.row_bytes + 15) & ~15ull) - g0);
+        const uint32_t ub = (uint32_t)(((u + (uint64_t)np * s.row_bytes + 15) & ~15ull) - u0);
+        if (pf) {
+            bulk_prefetch_l2(reinterpret_cast<const void *>(g0), gb);
+            bulk_prefetch_l2(reinterpret_cast<const void *>(u0), ub);
+            return;
+        }
+        mbar_arrive_expect_tx(&full[slot], gb + ub);
+        bulk_g2s(dst, reinterpret_cast<const void *>(g0), gb, &full[slot]);
+        bulk_g2s(dst + stage_bytes / 2, reinterpret_cast<const void *>(u0), ub, &full[slot]);
+    }
+}
+
+// Issue global stage j of this CTA.  The phase holding j is found by
+// scanning forward from a shared cursor: refills come in increasing j, so the
+// scan is normally zero or one step.  Concurrent refills may race on the
+// cursor; it then only lags behind, which keeps the scan correct.
+__device__ __forceinline__ void issue_global(const StageSrc *tab, uint32_t n_ph, uint32_t j, uint8_t *ring,
+                                             uint32_t stage_bytes, uint64_t *full, uint32_t slot,
+                                             uint32_t *cursor) {
+    uint32_t p = *(volatile uint32_t *)cursor;
+    if (p >= n_ph || tab[p].first > j) p = 0;  // defensive restart
+    while (p + 1 < n_ph && (tab[p].n_st == 0 || j >= tab[p].first + tab[p].n_st)) ++p;
+    atomicMax(cursor, p);
+    issue_src(tab[p], j - tab[p].first, ring, stage_bytes, full, slot);
+}
+
+struct PhaseResult {
+    RingState rs;
+    bool ok;
+};
+
+// Grid-wide barrier number `epoch` (1, 2, ...).  Bounded: on timeout, or
+// when another CTA already gave up, it sets the abort flag and returns false.
+__device__ bool grid_sync(uint32_t *sync, uint32_t epoch, uint32_t *err) {
+    __shared__ uint32_t ok_flag;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        // release: this CTA's writes of the phase become visible with the add;
+        // acquire: the other CTAs' writes are visible once the count is seen
+        red_release_add(&sync[0], 1u);
+        const uint32_t target = epoch * gridDim.x;
+        uint32_t ok = 0;
+        for (uint32_t i = 0; i < (1u << 25); ++i) {
+            if (ld_acquire(&sync[0]) >= target) { ok = 1; break; }
+            if ((i & 255) == 255) {
+                if (ld_acquire(&sync[1])) break;
+                __nanosleep(32);
+            }
+        }
+        if (!ok) {
+            atomicOr(err, ERR_GRID_SYNC);
+            atomicExch(&sync[1], 1u);
+        }
+        ok_flag = ok;
+    }
+    __syncthreads();
+    return ok_flag != 0;
+}
+
+template <int HD, int GQ>
+__device__ __noinline__ void attn_phase_t(const AttnArgs &a, uint8_t *scratch) {
+    auto &sh = *reinterpret_cast<AttnSmem<HD, GQ, kDecodeThreads / 32> *>(scratch);
+    const uint32_t n_pos = __ldcg(&a.step[1]) + 1;
+    const uint32_t n_use = attn_splits_in_use(a, n_pos);
+    const uint32_t n_kv = a.n_kv;
+    for (uint32_t it = blockIdx.x; it < n_kv * n_use; it += gridDim.x)
+        attn_item<HD, GQ, kDecodeThreads / 32>(a, it / n_use, it % n_use, n_pos, n_use, sh);
+}
+
+__device__ void attn_phase(const Phase &P, uint8_t *scratch) {
+#define FWB_ATTN(HDv, GQv) \
+    if (P.hd == HDv && P.gq == GQv) { attn_phase_t<HDv, GQv>(P.at, scratch); return; }
+    FWB_ATTN(128, 4) FWB_ATTN(128, 8) FWB_ATTN(128, 2) FWB_ATTN(128, 1)
+    FWB_ATTN(64, 1) FWB_ATTN(64, 2) FWB_ATTN(64, 4) FWB_ATTN(64, 8)
+    FWB_ATTN(48, 1) FWB_ATTN(48, 2) FWB_ATTN(48, 4) FWB_ATTN(48, 8)
+    FWB_ATTN(32, 1) FWB_ATTN(32, 2) FWB_ATTN(32, 4) FWB_ATTN(32, 8)
+#undef FWB_ATTN
+}
+
+// One GEMV phase.  Everything the hot loop touches is passed by value so it
+// stays in registers (a reference would force the struct into local memory).
+// One instantiation per (quant type, 4-byte alignment): the mode only changes
+// the prologue / epilogue and the pairing only per-thread offsets, so a model
+// with one quant type runs one copy of the row loop for every GEMV phase
+// (instruction-cache footprint).
+template <int QT, bool A4>
+__device__ __noinline__ PhaseResult gemv_phase_t(const GemvArgs *g, GemvSmem sm, RingState rs, const StageSrc *tab,
+                                                 uint32_t n_ph, uint32_t total, uint32_t NS, uint32_t stage_bytes) {
+    uint8_t *ring = sm.ring;
+    uint64_t *full = sm.full;
+    uint32_t *cursor = sm.done + kMaxStages;  // phase cursor word, next to the counters
+    auto refill = [=](uint32_t j, uint32_t slot) {
+        if (j + NS < total) issue_global(tab, n_ph, j + NS, ring, stage_bytes, full, slot, cursor);
+    };
+    PhaseResult r;
+    r.ok = gemv_consume<QT, A4>(*g, sm, threadIdx.x, rs, refill);
+    r.rs = rs;
+    return r;
+}
+
+template <int QT>
+__device__ PhaseResult gemv_phase_q(const Phase &P, const GemvSmem &sm, const RingState &rs, const StageSrc *tab,
+                                    uint32_t n_ph, uint32_t total, uint32_t NS, uint32_t stage_bytes) {
+    return P.a4 ? gemv_phase_t<QT, true>(&P.g, sm, rs, tab, n_ph, total, NS, stage_bytes)
+                : gemv_phase_t<QT, false>(&P.g, sm, rs, tab, n_ph, total, NS, stage_bytes);
+}
+
+__global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_constant__ DecodeArgs d) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const uint32_t tid = threadIdx.x;
+    const uint32_t ring_off = kHeaderBytes + d.scratch_bytes;
+    GemvSmem sm = gemv_smem(smem, 32);
+    sm.ring = smem + ring_off;
+    StageSrc *tab = reinterpret_cast<StageSrc *>(smem + ring_off + d.NS * d.stage_bytes + 128);
+    const uint32_t total = d.n_st_cta[blockIdx.x];
+
+    // this CTA's stream table -> shared memory
+    {
+        const uint32_t words = d.n_ph * (uint32_t)(sizeof(StageSrc) / 4);
+        const uint32_t *g = reinterpret_cast<const uint32_t *>(d.src + (size_t)blockIdx.x * d.n_ph);
+        uint32_t *s = reinterpret_cast<uint32_t *>(tab);
+        for (uint32_t i = tid; i < words; i += blockDim.x) s[i] = g[i];
+    }
+    if (tid == 0) {
+        for (uint32_t i = 0; i < d.NS; ++i) {
+            mbar_init(&sm.full[i], 1);
+            sm.done[i] = 0;
+        }
+        sm.done[kMaxStages] = 0;  // phase cursor of the refills
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (tid == 0) {
+        for (uint32_t j = 0; j < min(d.NS, total); ++j)
+            issue_global(tab, d.n_ph, j, sm.ring, d.stage_bytes, sm.full, j, sm.done + kMaxStages);
+    }
+
+    RingState rs{0, 0, 0};
+    bool ok = true;
+    // phase descriptors are staged in shared memory one phase ahead
+    __shared__ __align__(16) Phase ph_buf[2];
+    constexpr uint32_t kPhWords = sizeof(Phase) / 4;
+    for (uint32_t i = tid; i < kPhWords; i += blockDim.x)
+        reinterpret_cast<uint32_t *>(&ph_buf[0])[i] = reinterpret_cast<const uint32_t *>(d.ph)[i];
+    __syncthreads();
+    for (uint32_t p = 0; p < d.n_ph; ++p) {
+        const Phase &P = ph_buf[p & 1];
+        if (p + 1 < d.n_ph)
+            for (uint32_t i = tid; i < kPhWords; i += blockDim.x)
+                reinterpret_cast<uint32_t *>(&ph_buf[(p + 1) & 1])[i] =
+                    reinterpret_cast<const uint32_t *>(d.ph + p + 1)[i];
+        if (d.trace && blockIdx.x == 0 && tid == 0) d.trace[2 * p] = global_ns();
+        if (ok && !__ldcg(&d.sync[1])) {
+            if (P.kind == PH_GEMV) {
+                sm.planes = reinterpret_cast<uint32_t *>(smem + kHeaderBytes);
+                sm.nbp = ((P.g.K / 32) + 1) & ~1u;
+                PhaseResult r{rs, false};
+                switch (P.qt) {
+                case QT_Q4_0: r = gemv_phase_q<QT_Q4_0>(P, sm, rs, tab, d.n_ph, total, d.NS, d.stage_bytes); break;
+                case QT_Q5_0: r = gemv_phase_q<QT_Q5_0>(P, sm, rs, tab, d.n_ph, total, d.NS, d.stage_bytes); break;
+                case QT_Q8_0: r = gemv_phase_q<QT_Q8_0>(P, sm, rs, tab, d.n_ph, total, d.NS, d.stage_bytes); break;
+                default: break;
+                }
+                rs = r.rs;
+                ok = ok && r.ok;
+            } else if (P.kind == PH_ATTN) {
+                attn_phase(P, smem + kHeaderBytes);
+            } else {  // PH_EMBED: x = row step[0] of the table (linear_get_row, linear.c:60-151)
+                const EmbedArgs &e = P.e;
+                const uint32_t tok = __ldcg(&e.step[0]);
+                const uint8_t *row = e.table + (uint64_t)tok * e.row_bytes;
+                const uint32_t bb = e.type == 2 ? 18 : e.type == 6 ? 22 : 34;
+                for (uint32_t i = blockIdx.x * blockDim.x + tid; i < e.cols; i += gridDim.x * blockDim.x)
+                    e.x[i] = e.type == 0 ? reinterpret_cast<const float *>(row)[i]
+                                         : decode_value(row + (i >> 5) * bb, e.type, i & 31);
+            }
+        } else if (P.kind == PH_GEMV) {
+            // aborted: still walk the ring so that every issued stage is
+            // accounted for, without computing
+            ok = false;
+        }
+        if (d.trace && blockIdx.x == 0) {
+            __syncthreads();
+            if (tid == 0) d.trace[2 * p + 1] = global_ns();
+        }
+        if (p + 1 < d.n_ph && !grid_sync(d.sync, p + 1, d.err)) ok = false;
+    }
+    if (d.trace && blockIdx.x == 0 && tid == 0) d.trace[2 * d.n_ph] = global_ns();
+    if (!ok && tid == 0) ring_drain(sm, min(total, rs.j + d.NS), d.NS, d.err);
+}
+
+}  // namespace fwb

@@ -15,14 +15,19 @@
 // while the previous kernel of the decode step is still running.
 //
 // Arithmetic.  Consumer thread (slot s, unit u) owns columns [64u, 64u+64)
-// of one row per round.  Its 64 inputs are held in registers as 22-bit
-// fixed-point integers per 32-block (scale s_b = max|x_b| / (2^21-1)), split
-// into three byte planes, so each quant byte feeds dp4a directly:
-//   block dot = d * s_b * (256*(256*A + B) + C - off * sum(xi))
-// with A, B, C exact integer dot products of the quants with the high
-// (signed), middle and low byte planes.  The products and sums are exact; the
-// only rounding is the input's fixed-point representation (relative 2.4e-7
-// of the block maximum) and three final float operations per block.
+// of RPT rows per round (independent instruction streams).  Its 64 inputs are
+// held in registers as 16-bit fixed-point integers per 32-block (scale
+// s_b = max|x_b| / 32767), split into two byte planes, so each quant byte
+// feeds dp4a directly:
+//   block dot = d * s_b * (256*A + B - off * sum(xi))
+// with A, B exact integer dot products of the quants with the high (signed)
+// and low byte planes, accumulated by dp4a on top of the bit pattern of
+// 1.5*2^23 so that reading the accumulator as a float and subtracting
+// 1.5*2^23 converts it exactly (|A|, |B| < 2^22) without an int-to-float
+// instruction.  The products and sums are exact; the only rounding is the
+// input's fixed-point representation (at most 1.5e-5 of the block maximum
+// per value; about 3e-6 relative on a block dot of typical inputs) and a few
+// final float operations per block.
 //
 // Reduction.  Rows are processed in batches of 8 rounds; the 8 partial sums
 // per thread are reduced across the unit lanes with a butterfly
@@ -35,9 +40,14 @@ namespace fwb {
 
 enum QType : int { QT_Q4_0 = 2, QT_Q5_0 = 6, QT_Q8_0 = 8 };
 template <int QT> struct QTraits;
-template <> struct QTraits<QT_Q4_0> { static constexpr int BB = 18, OFF = 8; };
-template <> struct QTraits<QT_Q5_0> { static constexpr int BB = 22, OFF = 16; };
-template <> struct QTraits<QT_Q8_0> { static constexpr int BB = 34, OFF = 0; };
+// BB block bytes, OFF quant offset, RPT rows per thread per round (two
+// independent rows where registers allow; Q8_0's 34-byte blocks need more
+// registers per row and stream twice the bytes per value, so one row)
+template <> struct QTraits<QT_Q4_0> { static constexpr int BB = 18, OFF = 8, RPT = 2; };
+template <> struct QTraits<QT_Q5_0> { static constexpr int BB = 22, OFF = 16, RPT = 2; };
+template <> struct QTraits<QT_Q8_0> { static constexpr int BB = 34, OFF = 0, RPT = 1; };
+
+__host__ __device__ constexpr uint32_t rows_per_thread(int qt) { return qt == QT_Q8_0 ? 1u : 2u; }
 
 enum GemvMode : int {
     GM_STORE = 0,   // y[r]  = (W x)[r]
@@ -48,13 +58,16 @@ enum GemvMode : int {
 };
 enum InMode : int { IN_PLAIN = 0, IN_RMSNORM = 1 };
 
-constexpr int kRB = 8;              // rows per reduction batch (per slot)
+constexpr int kRB = 8;              // rows per reduction batch (per slot): 4 rounds x 2 rows
 constexpr int kMaxStages = 8;
+constexpr uint32_t kMaxConsumers = 512;  // threads per GEMV CTA (all consumers)
 constexpr uint32_t kHeaderBytes = 4096;
 constexpr uint32_t kStageSlack = 128;  // alignment + half-unit over-read room
-constexpr int kXMax = 2097151;      // 2^21 - 1, fixed-point range of the inputs
+constexpr int kXMax = 32767;        // fixed-point range of the inputs (16 bits per value)
 
 struct GemvArgs {
+    uint32_t mode;       // GemvMode (the row loop is shared; only prologue/epilogue differ)
+    uint32_t norm;       // 1: RMSNorm the input (IN_RMSNORM)
     const uint8_t *w;    // rows of the weight matrix (SWIGLU: gate)
     const uint8_t *w2;   // SWIGLU: up
     uint32_t n_out;      // output rows (SWIGLU: pairs)
@@ -77,69 +90,53 @@ struct GemvArgs {
     float *am_val;
     uint32_t *am_idx, *ticket, *out_token;
     const uint32_t *step;  // [0] token, [1] pos
+    uint32_t *step_rw, *hist;  // GM_LOGITS: advance step[0..1], record hist[pos]
     uint32_t *err;
+    // optional profile: thread 0 of each CTA adds ns spent in
+    // [0] prologue (norm + planes), [1] waiting for stages, [2] the row loop, [3] tail
+    unsigned long long *prof;
 };
+
+__device__ __forceinline__ unsigned long long gtime_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
 
 // ---------------------------------------------------------------------------
 // input planes
 // ---------------------------------------------------------------------------
 struct XBlock {
-    uint32_t hi[8], mid[8], lo[8];  // 4 elements per word, element order 4k..4k+3
-    int nx;                         // -OFF * sum(xi)
+    uint32_t hi[8], lo[8];          // 4 elements per word, element order 4k..4k+3
+    float nx;                       // -OFF * sum(xi)
     float s;                        // s_b
 };
 
-template <int OFF>
-__device__ __forceinline__ void quantize_block(const float *v, XBlock &b) {
-    float m = 0.f;
-    bool bad = false;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-        m = fmaxf(m, fabsf(v[j]));
-        bad |= !isfinite(v[j]);
-    }
-    const float inv = m > 0.f ? (float)kXMax / m : 0.f;
-    b.s = bad ? __int_as_float(0x7fc00000) : m * (1.0f / (float)kXMax);
-    int sum = 0;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-        int xi[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            int t = __float2int_rn(v[4 * k + e] * inv);
-            xi[e] = max(-kXMax, min(kXMax, t));
-            sum += xi[e];
-        }
-        b.lo[k] = __byte_perm(__byte_perm(xi[0], xi[1], 0x0040), __byte_perm(xi[2], xi[3], 0x0040), 0x5410);
-        b.mid[k] = __byte_perm(__byte_perm(xi[0], xi[1], 0x0051), __byte_perm(xi[2], xi[3], 0x0051), 0x5410);
-        b.hi[k] = __byte_perm(__byte_perm(xi[0], xi[1], 0x0062), __byte_perm(xi[2], xi[3], 0x0062), 0x5410);
-    }
-    b.nx = -OFF * sum;
-}
+constexpr int kMagicBits = 0x4B400000;      // 1.5 * 2^23 as fp32 bits
+constexpr float kMagic = 12582912.0f;
 
 // ---------------------------------------------------------------------------
 // block dots
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ float finish_block(int A, int B, int C, const XBlock &x, uint32_t dbits) {
-    const int U = A * 256 + B;
-    const float T = fmaf((float)U, 256.0f, (float)(C + x.nx));
+// A, B carry the kMagicBits bias (see the header comment)
+__device__ __forceinline__ float finish_block(int A, int B, const XBlock &x, uint32_t dbits) {
+    const float Af = __int_as_float(A) - kMagic, Bf = __int_as_float(B) - kMagic;
+    const float T = fmaf(Af, 256.0f, Bf) + x.nx;
     return (f16_bits_to_f32(dbits) * x.s) * T;
 }
 
 // Q4_0: 4 quant words (elements 4k..4k+3 in the low nibbles, 16+4k.. in the high)
 __device__ __forceinline__ float dot_q4_0(const uint32_t (&q)[4], uint32_t dbits, const XBlock &x) {
-    int A = 0, B = 0, C = 0;
+    int A = kMagicBits, B = kMagicBits;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         const uint32_t lo = q[k] & 0x0F0F0F0Fu, hi = (q[k] >> 4) & 0x0F0F0F0Fu;
         A = dp4a_us(lo, (int)x.hi[k], A);
         A = dp4a_us(hi, (int)x.hi[k + 4], A);
-        B = dp4a_uu(lo, x.mid[k], B);
-        B = dp4a_uu(hi, x.mid[k + 4], B);
-        C = dp4a_uu(lo, x.lo[k], C);
-        C = dp4a_uu(hi, x.lo[k + 4], C);
+        B = dp4a_uu(lo, x.lo[k], B);
+        B = dp4a_uu(hi, x.lo[k + 4], B);
     }
-    return finish_block(A, B, C, x, dbits);
+    return finish_block(A, B, x, dbits);
 }
 
 // spread 4 bits into bit 4 of each byte
@@ -147,31 +144,28 @@ __device__ __forceinline__ uint32_t spread4(uint32_t b) { return ((b & 0xFu) * 0
 
 // Q5_0: qh = 32-bit high-bit plane (bit j of element j), 4 low-nibble words
 __device__ __forceinline__ float dot_q5_0(uint32_t qh, const uint32_t (&q)[4], uint32_t dbits, const XBlock &x) {
-    int A = 0, B = 0, C = 0;
+    int A = kMagicBits, B = kMagicBits;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         const uint32_t lo = (q[k] & 0x0F0F0F0Fu) | spread4(qh >> (4 * k));
         const uint32_t hi = ((q[k] >> 4) & 0x0F0F0F0Fu) | spread4(qh >> (16 + 4 * k));
         A = dp4a_us(lo, (int)x.hi[k], A);
         A = dp4a_us(hi, (int)x.hi[k + 4], A);
-        B = dp4a_uu(lo, x.mid[k], B);
-        B = dp4a_uu(hi, x.mid[k + 4], B);
-        C = dp4a_uu(lo, x.lo[k], C);
-        C = dp4a_uu(hi, x.lo[k + 4], C);
+        B = dp4a_uu(lo, x.lo[k], B);
+        B = dp4a_uu(hi, x.lo[k + 4], B);
     }
-    return finish_block(A, B, C, x, dbits);
+    return finish_block(A, B, x, dbits);
 }
 
 // Q8_0: 8 signed quant words
 __device__ __forceinline__ float dot_q8_0(const uint32_t (&q)[8], uint32_t dbits, const XBlock &x) {
-    int A = 0, B = 0, C = 0;
+    int A = kMagicBits, B = kMagicBits;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
         A = dp4a_ss((int)q[k], (int)x.hi[k], A);
-        B = dp4a_su((int)q[k], x.mid[k], B);
-        C = dp4a_su((int)q[k], x.lo[k], C);
+        B = dp4a_su((int)q[k], x.lo[k], B);
     }
-    return finish_block(A, B, C, x, dbits);
+    return finish_block(A, B, x, dbits);
 }
 
 // Words of one unit (two blocks, 2*BB bytes) starting at p (2-byte aligned;
@@ -278,222 +272,351 @@ __device__ __forceinline__ void cta_rows(uint32_t n_out, uint32_t g, uint32_t &b
 }
 
 // ---------------------------------------------------------------------------
-// the kernel
+// one GEMV, split into a producer (one thread) and consumers (NC threads).
+// Stage k of the CTA lives in ring slot kring % NS, phase parity
+// (kring / NS) & 1, where kring counts stages from the start of the ring, so
+// several GEMVs can run back to back through one ring.
 // ---------------------------------------------------------------------------
-template <int QT, int MODE, int IN, bool A4, int MAXT, int MINB>
-__global__ void __launch_bounds__(MAXT, MINB) gemv_kernel(const __grid_constant__ GemvArgs a) {
-    constexpr int BB = QTraits<QT>::BB;
-    constexpr int OFF = QTraits<QT>::OFF;
-    constexpr bool PAIRED = (MODE == GM_SWIGLU);
-    extern __shared__ __align__(128) uint8_t smem[];
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
-    uint64_t *empty = full + kMaxStages;
-    float *red = reinterpret_cast<float *>(smem + 256);       // [8][32]
-    float *out_tile = red + kRB * 32;                         // [<= 8 * 64 pairs...] 512
-    float *misc = out_tile + 512;                             // 64
-    uint32_t *misc_u = reinterpret_cast<uint32_t *>(misc + 64);  // 64
-    uint8_t *ring = smem + kHeaderBytes;
 
-    const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const uint32_t NC = a.NC, NCW = NC >> 5;
+struct GemvSmem {
+    uint64_t *full;   // [kMaxStages] stage landed (transaction count)
+    uint32_t *done;   // [kMaxStages] consumer warps finished with the slot
+    float *red, *out_tile, *misc;
+    uint32_t *misc_u;
+    uint32_t *planes;  // quantised input: word (p*8+k)*nbp + b (p 0 = high, 1 = low), s at 16*nbp + b, nx at 17*nbp + b
+    uint32_t nbp;      // blocks of the input, rounded up to even
+    uint8_t *ring;
+};
 
-    uint32_t rb, re;  // CTA range in output rows (pairs for SWIGLU)
-    cta_rows(a.n_out, a.gran, rb, re);
-    const uint32_t n_loc = PAIRED ? 2 * (re - rb) : (re - rb);  // local rows
-    const uint32_t R = a.R, NS = a.NS;
-    const uint32_t n_st = (n_loc + R - 1) / R;
+// Bytes of the plane area for an input of K values.
+__host__ __device__ constexpr uint32_t plane_bytes(uint32_t K) {
+    return ((18u * (((K / 32) + 1) & ~1u) * 4u) + 127u) & ~127u;
+}
 
-    if (tid == 0) {
-        for (uint32_t i = 0; i < NS; ++i) {
-            mbar_init(&full[i], 1);
-            mbar_init(&empty[i], NCW);
-        }
-        fence_mbar_init();
+__device__ __forceinline__ GemvSmem gemv_smem(uint8_t *smem, uint32_t K) {
+    GemvSmem g;
+    g.full = reinterpret_cast<uint64_t *>(smem);
+    g.done = reinterpret_cast<uint32_t *>(g.full + kMaxStages);
+    g.red = reinterpret_cast<float *>(smem + 256);    // [8][32]
+    g.out_tile = g.red + kRB * 32;                    // [512]
+    g.misc = g.out_tile + 512;                        // [64]
+    g.misc_u = reinterpret_cast<uint32_t *>(g.misc + 64);  // [64]
+    g.planes = reinterpret_cast<uint32_t *>(smem + kHeaderBytes);
+    g.nbp = ((K / 32) + 1) & ~1u;
+    g.ring = smem + kHeaderBytes + plane_bytes(K);
+    return g;
+}
+
+// Issue the bulk copy of local stage k of this CTA's rows into ring slot
+// `slot` (one thread).  Rows are copied as 16-byte-aligned supersets; the
+// consumer recomputes the same offset (delta) from the row address.
+template <bool PAIRED>
+__device__ __forceinline__ void issue_stage(const GemvArgs &a, const GemvSmem &sm, uint32_t rb, uint32_t re,
+                                            uint32_t k, uint32_t slot) {
+    const uint32_t R = a.R;
+    uint8_t *dst = sm.ring + (size_t)slot * a.stage_bytes;
+    if (!PAIRED) {
+        const uint32_t n_loc = re - rb;
+        const uint32_t r0 = k * R, nr = min(R, n_loc - r0);
+        const uintptr_t src = reinterpret_cast<uintptr_t>(a.w) + (uint64_t)(rb + r0) * a.row_bytes;
+        const uintptr_t s0 = src & ~uintptr_t(15);
+        const uint32_t bytes = (uint32_t)(((src + (uint64_t)nr * a.row_bytes + 15) & ~uintptr_t(15)) - s0);
+        mbar_arrive_expect_tx(&sm.full[slot], bytes);
+        bulk_g2s(dst, reinterpret_cast<const void *>(s0), bytes, &sm.full[slot]);
+    } else {
+        const uint32_t p0 = k * (R / 2), np = min(R / 2, (re - rb) - p0);
+        const uint64_t off = (uint64_t)(rb + p0) * a.row_bytes;
+        const uintptr_t g = reinterpret_cast<uintptr_t>(a.w) + off;
+        const uintptr_t u = reinterpret_cast<uintptr_t>(a.w2) + off;
+        const uintptr_t g0 = g & ~uintptr_t(15), u0 = u & ~uintptr_t(15);
+        const uint32_t gb = (uint32_t)(((g + (uint64_t)np * a.row_bytes + 15) & ~uintptr_t(15)) - g0);
+        const uint32_t ub = (uint32_t)(((u + (uint64_t)np * a.row_bytes + 15) & ~uintptr_t(15)) - u0);
+        mbar_arrive_expect_tx(&sm.full[slot], gb + ub);
+        bulk_g2s(dst, reinterpret_cast<const void *>(g0), gb, &sm.full[slot]);
+        bulk_g2s(dst + a.stage_bytes / 2, reinterpret_cast<const void *>(u0), ub, &sm.full[slot]);
     }
-    __syncthreads();
-    pdl_launch();
+}
 
-    // ------------------------------------------------------------ producer
-    if (warp == NCW) {
-        if (lane != 0) return;
-        uint32_t issued = 0;
-        bool failed = false;
-        for (uint32_t k = 0; k < n_st; ++k) {
-            const uint32_t s = k % NS;
-            if (k >= NS && !mbar_wait(&empty[s], ((k / NS) - 1) & 1, a.err, ERR_WAIT_EMPTY)) {
-                failed = true;
-                break;
+// Stages of this CTA: one per round of R = RPT * S local rows.
+template <bool PAIRED>
+__device__ __forceinline__ uint32_t n_stages_of(const GemvArgs &a, uint32_t rb, uint32_t re) {
+    const uint32_t n_loc = PAIRED ? 2 * (re - rb) : (re - rb);
+    return (n_loc + a.R - 1) / a.R;
+}
+
+// Ring position of the next stage a consumer will read: slot, phase parity,
+// and the stage's index j (local to one GEMV in the standalone kernel, global
+// across all phases in the persistent decode kernel).
+struct RingState {
+    uint32_t slot, par, j;
+};
+
+// Called by lane 0 of every warp when it is done with stage rs.j: the last
+// warp to finish hands the slot to `refill`, which issues stage j + NS into
+// it (if such a stage exists).
+template <class Refill>
+__device__ __forceinline__ void ring_release(const GemvSmem &sm, const RingState &rs, uint32_t nwarps,
+                                             const Refill &refill) {
+    __threadfence_block();
+    if (atomicAdd(&sm.done[rs.slot], 1u) == nwarps - 1) {
+        sm.done[rs.slot] = 0;
+        __threadfence_block();
+        refill(rs.j, rs.slot);
+    }
+}
+
+__device__ __forceinline__ void ring_advance(RingState &rs, uint32_t NS) {
+    ++rs.j;
+    if (++rs.slot == NS) { rs.slot = 0; rs.par ^= 1u; }
+}
+
+// Quantise the input vector once per CTA into the shared plane area: a group
+// of 4 lanes per 32-block, 8 values per lane (RMSNorm applied when
+// IN_RMSNORM; `scale` is its factor).  Float -> int by adding 1.5*2^23
+// (exact round-to-nearest for |v| < 2^22).
+template <int OFF>
+__device__ void build_planes(const GemvArgs &a, const GemvSmem &sm, uint32_t tid, uint32_t NC, float scale) {
+    const bool norm = a.norm != 0;
+    const uint32_t nb = a.K >> 5, nbp = sm.nbp;
+    const uint32_t q = tid & 3;
+    for (uint32_t b = tid >> 2; b < ((nb + 7) & ~7u); b += NC >> 2) {  // whole warps iterate together
+        const bool on = b < nb;
+        float v[8];
+        const uint32_t c = b * 32 + q * 8;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (on) {
+                t = __ldcg(reinterpret_cast<const float4 *>(a.x + c + 4 * h));  // written by other CTAs
+                if (norm) {
+                    const float4 w = *reinterpret_cast<const float4 *>(a.norm_w + c + 4 * h);
+                    t.x = __fmul_rn(__fmul_rn(t.x, w.x), scale);
+                    t.y = __fmul_rn(__fmul_rn(t.y, w.y), scale);
+                    t.z = __fmul_rn(__fmul_rn(t.z, w.z), scale);
+                    t.w = __fmul_rn(__fmul_rn(t.w, w.w), scale);
+                }
             }
-            uint8_t *dst = ring + (size_t)s * a.stage_bytes;
-            if (!PAIRED) {
-                const uint32_t r0 = k * R, nr = min(R, n_loc - r0);
-                const uintptr_t src = reinterpret_cast<uintptr_t>(a.w) + (uint64_t)(rb + r0) * a.row_bytes;
-                const uintptr_t s0 = src & ~uintptr_t(15);
-                const uint32_t bytes = (uint32_t)(((src + (uint64_t)nr * a.row_bytes + 15) & ~uintptr_t(15)) - s0);
-                mbar_arrive_expect_tx(&full[s], bytes);
-                bulk_g2s(dst, reinterpret_cast<const void *>(s0), bytes, &full[s]);
-            } else {
-                const uint32_t p0 = k * (R / 2), np = min(R / 2, (re - rb) - p0);
-                const uint64_t off = (uint64_t)(rb + p0) * a.row_bytes;
-                const uintptr_t g = reinterpret_cast<uintptr_t>(a.w) + off;
-                const uintptr_t u = reinterpret_cast<uintptr_t>(a.w2) + off;
-                const uintptr_t g0 = g & ~uintptr_t(15), u0 = u & ~uintptr_t(15);
-                const uint32_t gb = (uint32_t)(((g + (uint64_t)np * a.row_bytes + 15) & ~uintptr_t(15)) - g0);
-                const uint32_t ub = (uint32_t)(((u + (uint64_t)np * a.row_bytes + 15) & ~uintptr_t(15)) - u0);
-                mbar_arrive_expect_tx(&full[s], gb + ub);
-                bulk_g2s(dst, reinterpret_cast<const void *>(g0), gb, &full[s]);
-                bulk_g2s(dst + a.stage_bytes / 2, reinterpret_cast<const void *>(u0), ub, &full[s]);
+            v[4 * h] = t.x; v[4 * h + 1] = t.y; v[4 * h + 2] = t.z; v[4 * h + 3] = t.w;
+        }
+        float m = 0.f, chk = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            m = fmaxf(m, fabsf(v[j]));
+            chk += v[j];  // NaN / inf propagate here (fmaxf would drop NaN)
+        }
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+        const bool bad = !isfinite(chk) || !isfinite(m);
+        const float inv = m > 1e-30f && !bad ? (float)kXMax / m : 0.f;
+        int xi[8], sum = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            xi[j] = __float_as_int(fmaf(v[j], inv, kMagic)) - kMagicBits;
+            sum += xi[j];
+        }
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        if (on) {
+#pragma unroll
+            for (int w = 0; w < 2; ++w) {
+                const int *x4 = xi + 4 * w;
+                // |xi| <= 32767: byte 0 is the low plane, byte 1 the signed high plane
+                const uint32_t t01 = __byte_perm(x4[0], x4[1], 0x5140), t23 = __byte_perm(x4[2], x4[3], 0x5140);
+                const uint32_t lo = __byte_perm(t01, t23, 0x5410), hi = __byte_perm(t01, t23, 0x7632);
+                const uint32_t k = 2 * q + w;
+                sm.planes[(0 * 8 + k) * nbp + b] = hi;
+                sm.planes[(1 * 8 + k) * nbp + b] = lo;
             }
-            ++issued;
+            if (q == 0) {
+                sm.planes[16 * nbp + b] = __float_as_uint(bad ? __int_as_float(0x7fc00000)
+                                                              : (m > 1e-30f ? m * (1.0f / (float)kXMax) : 0.f));
+                sm.planes[17 * nbp + b] = __float_as_uint((float)(-OFF) * (float)sum);
+            }
         }
-        if (failed) {  // drain copies still in flight before the CTA may exit
-            const uint32_t k0 = issued > NS ? issued - NS : 0;
-            for (uint32_t k = k0; k < issued; ++k)
-                mbar_wait(&full[k % NS], (k / NS) & 1, a.err, ERR_WAIT_DRAIN);
-        }
+    }
+}
+
+// This thread's two input blocks (2u, 2u+1) from the plane area.
+__device__ __forceinline__ void load_planes(const GemvSmem &sm, uint32_t unit, bool active, XBlock &xa, XBlock &xb) {
+    const uint32_t nbp = sm.nbp, b = 2 * unit;
+    if (!active) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) { xa.hi[k] = xa.lo[k] = xb.hi[k] = xb.lo[k] = 0; }
+        xa.s = xb.s = xa.nx = xb.nx = 0.f;
         return;
     }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const uint2 h = *reinterpret_cast<const uint2 *>(sm.planes + (0 * 8 + k) * nbp + b);
+        const uint2 l = *reinterpret_cast<const uint2 *>(sm.planes + (1 * 8 + k) * nbp + b);
+        xa.hi[k] = h.x; xb.hi[k] = h.y;
+        xa.lo[k] = l.x; xb.lo[k] = l.y;
+    }
+    const uint2 sv = *reinterpret_cast<const uint2 *>(sm.planes + 16 * nbp + b);
+    const uint2 nv = *reinterpret_cast<const uint2 *>(sm.planes + 17 * nbp + b);
+    xa.s = __uint_as_float(sv.x); xb.s = __uint_as_float(sv.y);
+    xa.nx = __uint_as_float(nv.x); xb.nx = __uint_as_float(nv.y);
+}
 
-    // ------------------------------------------------------------ consumers
+// RMSNorm factor over a.x (rms_norm, norm.c:7-16):
+// 1/sqrtf(sum(x^2)/n + eps), IEEE division and square root.
+__device__ float rms_scale(const GemvArgs &a, const GemvSmem &sm, uint32_t tid, uint32_t NC) {
+    const uint32_t lane = tid & 31, warp = tid >> 5, NCW = NC >> 5;
+    float ss = 0.f;
+    for (uint32_t i = tid * 4; i < a.K; i += NC * 4) {
+        const float4 t = __ldcg(reinterpret_cast<const float4 *>(a.x + i));
+        ss = fmaf(t.x, t.x, ss);
+        ss = fmaf(t.y, t.y, ss);
+        ss = fmaf(t.z, t.z, ss);
+        ss = fmaf(t.w, t.w, ss);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) sm.misc[warp] = ss;
+    bar_sync(1, NC);
+    if (warp == 0) {
+        float t = lane < NCW ? sm.misc[lane] : 0.f;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+        if (lane == 0) sm.misc[32] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)a.K), a.eps)));
+    }
+    bar_sync(1, NC);
+    const float r = sm.misc[32];
+    bar_sync(1, NC);
+    return r;
+}
+
+// Consumers: returns false if a bounded wait failed (results then invalid).
+template <int QT, bool A4, class Refill>
+__device__ bool gemv_consume(const GemvArgs &a, const GemvSmem &sm, uint32_t tid, RingState &rs,
+                             const Refill &refill) {
+    // run-time: the mode only changes the prologue / epilogue, pairing only the
+    // per-thread row offsets (one copy of the row loop per quant type)
+    const uint32_t MODE = a.mode;
+    const bool PAIRED = MODE == GM_SWIGLU;
+    constexpr int BB = QTraits<QT>::BB;
+    constexpr int OFF = QTraits<QT>::OFF;
+    // a.NC threads carry (slot, unit) work; the whole block takes part in the
+    // ring protocol, barriers and epilogues
+    const uint32_t NC = blockDim.x, lane = tid & 31, warp = tid >> 5, NCW = NC >> 5;
+    uint32_t rb, re;
+    cta_rows(a.n_out, a.gran, rb, re);
+    const uint32_t n_loc = PAIRED ? 2 * (re - rb) : (re - rb);
     const uint32_t Upad = a.Upad, S = a.S, U = a.U;
     const uint32_t slot = tid / Upad, unit = tid % Upad;
     const uint32_t nb = a.K >> 5;
-    const bool active = slot < S && unit < U;
+    const bool active = tid < a.NC && slot < S && unit < U;
     const bool two = active && (2 * unit + 1 < nb);
     const uint32_t G = Upad < 32 ? Upad : 32;
+    constexpr uint32_t RPT = QTraits<QT>::RPT;
+    const uint32_t RS = RPT * S;  // local rows per round
 
-    pdl_wait();  // inputs of this GEMV are outputs of the previous kernel
-
-    // input vector -> fixed-point planes
-    float scale = 1.0f;
-    if (IN == IN_RMSNORM) {
-        // rms_norm, norm.c:7-16: scale = 1/sqrtf(sum(x^2)/n + eps); out = (x*w)*scale
-        float ss = 0.f;
-        for (uint32_t i = tid; i < a.K; i += NC) ss = fmaf(a.x[i], a.x[i], ss);
-#pragma unroll
-        for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        if (lane == 0) misc[warp] = ss;
-        bar_sync(1, NC);
-        if (warp == 0) {
-            float t = lane < NCW ? misc[lane] : 0.f;
-#pragma unroll
-            for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-            if (lane == 0) misc[32] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)a.K), a.eps)));
-        }
-        bar_sync(1, NC);
-        scale = misc[32];
-    }
+    const bool prof = a.prof != nullptr && tid == 0;
+    unsigned long long t0 = prof ? gtime_ns() : 0ull, t_wait = 0ull;
+    const float scale = a.norm ? rms_scale(a, sm, tid, NC) : 1.0f;
+    build_planes<OFF>(a, sm, tid, NC, scale);
+    bar_sync(1, NC);
+    unsigned long long t1 = prof ? gtime_ns() : 0ull;
     XBlock xa, xb;
-    {
-        float v[32];
-        const uint32_t c0 = unit * 64;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-            float t = 0.f;
-            if (active) {
-                t = a.x[c0 + j];
-                if (IN == IN_RMSNORM) t = __fmul_rn(__fmul_rn(t, a.norm_w[c0 + j]), scale);
-            }
-            v[j] = t;
-        }
-        quantize_block<OFF>(v, xa);
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-            float t = 0.f;
-            if (two) {
-                t = a.x[c0 + 32 + j];
-                if (IN == IN_RMSNORM) t = __fmul_rn(__fmul_rn(t, a.norm_w[c0 + 32 + j]), scale);
-            }
-            v[j] = t;
-        }
-        quantize_block<OFF>(v, xb);
-    }
+    load_planes(sm, unit, active, xa, xb);
 
-    const uint32_t n_rounds = (n_loc + S - 1) / S;
-    const uint32_t RPS = R / S;
-    uint32_t pos = 0;
-    if (MODE == GM_QKV) pos = a.step[1];
-    bool failed = false;
-
+    // One ring stage per round: stage k holds local rows [k*RS, (k+1)*RS).
+    const uint32_t n_rounds = (n_loc + RS - 1) / RS;
+    const uint32_t NS = a.NS, rbytes = a.row_bytes, sbytes = a.stage_bytes;
+    const uint32_t pos = MODE == GM_QKV ? __ldcg(&a.step[1]) : 0u;
+    bool ok = true;
     float best_v = -INFINITY;
     uint32_t best_i = 0xffffffffu;
+    // byte offset (inside a stage, before the alignment delta) of this
+    // thread's unit in each of its RPT rows; paired stages hold the gate rows
+    // in the first half and the up rows in the second, interleaved as
+    // local rows (gate, up, gate, up, ...)
+    uint32_t off[RPT];
+    bool up_half[RPT];
+    const uint32_t slot_c = min(slot, S - 1), unit_c = min(unit, U - 1);  // in-bounds for inactive threads
+#pragma unroll
+    for (uint32_t e = 0; e < RPT; ++e) {
+        const uint32_t ls = e * S + slot_c;
+        if (!PAIRED) {
+            off[e] = ls * rbytes + unit_c * (2 * BB);
+            up_half[e] = false;
+        } else {
+            off[e] = (ls >> 1) * rbytes + unit_c * (2 * BB) + ((ls & 1) ? sbytes / 2 : 0u);
+            up_half[e] = ls & 1;
+        }
+    }
+    // low 32 bits of the first source byte of the current stage (gate / up),
+    // advanced per stage; only the value mod 16 (the alignment delta) is used
+    uint32_t src_a = (uint32_t)(reinterpret_cast<uintptr_t>(a.w) + (uint64_t)rb * rbytes);
+    uint32_t src_b = PAIRED ? (uint32_t)(reinterpret_cast<uintptr_t>(a.w2) + (uint64_t)rb * rbytes) : 0u;
+    const uint32_t src_step = PAIRED ? (RS / 2) * rbytes : RS * rbytes;
+    const uint8_t *ring = sm.ring;
 
-    uint32_t stage = 0, in_stage = 0;  // stage index, round within stage
-    const uint8_t *sbase = ring;
-    uint32_t delta_a = 0, delta_b = 0;
-
-    for (uint32_t r0 = 0; r0 < n_rounds; r0 += kRB) {
+    for (uint32_t r0 = 0; r0 < n_rounds; r0 += kRB / RPT) {
         float acc[kRB];
 #pragma unroll
-        for (int j = 0; j < kRB; ++j) {
-            acc[j] = 0.f;
-            const uint32_t r = r0 + j;
+        for (int jj = 0; jj < kRB / (int)RPT; ++jj) {
+#pragma unroll
+            for (uint32_t e = 0; e < RPT; ++e) acc[RPT * jj + e] = 0.f;
+            const uint32_t r = r0 + jj;
             if (r < n_rounds) {
-                if (in_stage == 0) {
-                    const uint32_t s = stage % NS;
-                    if (!failed) failed = !mbar_wait(&full[s], (stage / NS) & 1, a.err, ERR_WAIT_FULL);
-                    sbase = ring + (size_t)s * a.stage_bytes;
-                    if (!PAIRED) {
-                        const uintptr_t src = reinterpret_cast<uintptr_t>(a.w) +
-                                              (uint64_t)(rb + stage * R) * a.row_bytes;
-                        delta_a = (uint32_t)(src & 15);
-                    } else {
-                        const uint64_t off = (uint64_t)(rb + stage * (R / 2)) * a.row_bytes;
-                        delta_a = (uint32_t)((reinterpret_cast<uintptr_t>(a.w) + off) & 15);
-                        delta_b = (uint32_t)((reinterpret_cast<uintptr_t>(a.w2) + off) & 15);
-                    }
+                if (prof) {
+                    const unsigned long long w0 = gtime_ns();
+                    if (ok) ok = mbar_wait(&sm.full[rs.slot], rs.par, a.err, ERR_WAIT_FULL);
+                    t_wait += gtime_ns() - w0;
+                } else if (ok) {
+                    ok = mbar_wait(&sm.full[rs.slot], rs.par, a.err, ERR_WAIT_FULL);
                 }
-                const uint32_t l = r * S + slot;  // local row
-                if (active && l < n_loc && !failed) {
-                    const uint32_t ls = l - stage * R;  // row within stage
-                    const uint8_t *rowp;
-                    if (!PAIRED) {
-                        rowp = sbase + delta_a + (size_t)ls * a.row_bytes;
-                    } else {
-                        const uint32_t pr = ls >> 1;
-                        rowp = (ls & 1) ? sbase + a.stage_bytes / 2 + delta_b + (size_t)pr * a.row_bytes
-                                        : sbase + delta_a + (size_t)pr * a.row_bytes;
-                    }
-                    acc[j] = unit_dot<QT, A4>(rowp + unit * (2 * BB), xa, xb, two);
+                // every thread computes (inactive ones on clamped, in-bounds
+                // addresses) so the body has no divergent branch
+                const uint8_t *sb = ring + rs.slot * sbytes;
+                float d[RPT];
+#pragma unroll
+                for (uint32_t e = 0; e < RPT; ++e) {
+                    const uint32_t delta = up_half[e] ? (src_b & 15u) : (src_a & 15u);
+                    d[e] = unit_dot<QT, A4>(sb + off[e] + delta, xa, xb, two);
                 }
-                if (++in_stage == RPS || r + 1 == n_rounds) {
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&empty[stage % NS]);
-                    in_stage = 0;
-                    ++stage;
-                }
+                const uint32_t lr = r * RS + slot;
+#pragma unroll
+                for (uint32_t e = 0; e < RPT; ++e) acc[RPT * jj + e] = (active && lr + e * S < n_loc) ? d[e] : 0.f;
+                __syncwarp();
+                if (lane == 0) ring_release(sm, rs, NCW, refill);
+                src_a += src_step;
+                src_b += src_step;
+                ring_advance(rs, NS);
             }
         }
 
-        // ---- reduce the batch
-        uint32_t jj;
-        const float v = reduce8(acc, lane, G, jj);
-        const uint32_t nbr = min((uint32_t)kRB, n_rounds - r0);
+        // ---- reduce: acc[i] belongs to local row (r0 + i/RPT)*RS + (i%RPT)*S + slot,
+        //      i.e. out_tile index (i/RPT)*RS + (i%RPT)*S + slot
+        uint32_t jj8;
+        const float v = reduce8(acc, lane, G, jj8);
+        const uint32_t tpos = (jj8 / RPT) * RS + (jj8 % RPT) * S;
         if (Upad <= 32) {
-            if ((lane & ((G >> 3) - 1)) == 0 && slot < S) out_tile[jj * S + slot] = v;
+            if ((lane & ((G >> 3) - 1)) == 0 && slot < S) sm.out_tile[tpos + slot] = v;
         } else {
-            if ((lane & 3) == 0) red[jj * 32 + warp] = v;
+            if ((lane & 3) == 0) sm.red[jj8 * 32 + warp] = v;
             bar_sync(1, NC);
             const uint32_t W = Upad >> 5;
             if (tid < kRB * S) {
                 const uint32_t j = tid % kRB, s = tid / kRB;
                 float t = 0.f;
-                for (uint32_t w = 0; w < W; ++w) t += red[j * 32 + s * W + w];
-                out_tile[j * S + s] = t;
+                for (uint32_t w = 0; w < W; ++w) t += sm.red[j * 32 + s * W + w];
+                sm.out_tile[(j / RPT) * RS + (j % RPT) * S + s] = t;
             }
         }
         bar_sync(1, NC);
 
-        // ---- epilogue on local rows [r0*S, r0*S + nbr*S) ∩ [0, n_loc)
-        const uint32_t l0 = r0 * S;
-        const uint32_t cnt = min(nbr * S, n_loc - l0);
-        if (!failed) {
+        // ---- epilogue on local rows [r0*RS, r0*RS + cnt)
+        const uint32_t l0 = r0 * RS;  // even: RS * (kRB / RPT) is even
+        const uint32_t cnt = min((uint32_t)(kRB / RPT) * RS, n_loc - l0);
+        if (ok) {
             if (MODE == GM_STORE || MODE == GM_RESID || MODE == GM_LOGITS) {
                 for (uint32_t i = tid; i < cnt; i += NC) {
                     const uint32_t g = rb + l0 + i;
-                    const float t = out_tile[i];
+                    const float t = sm.out_tile[i];
                     if (MODE == GM_STORE) a.y[g] = t;
-                    if (MODE == GM_RESID) a.y[g] = __fadd_rn(a.y[g], t);
+                    if (MODE == GM_RESID) a.y[g] = __fadd_rn(__ldcg(&a.y[g]), t);
                     if (MODE == GM_LOGITS) {
                         a.y[g] = t;
                         if (t > best_v || (t == best_v && g < best_i)) { best_v = t; best_i = g; }
@@ -502,13 +625,13 @@ __global__ void __launch_bounds__(MAXT, MINB) gemv_kernel(const __grid_constant_
             } else if (MODE == GM_SWIGLU) {
                 for (uint32_t i = tid; 2 * i < cnt; i += NC) {
                     const uint32_t p = rb + (l0 >> 1) + i;
-                    a.y[p] = __fmul_rn(silu_ref(out_tile[2 * i]), out_tile[2 * i + 1]);
+                    a.y[p] = __fmul_rn(silu_ref(sm.out_tile[2 * i]), sm.out_tile[2 * i + 1]);
                 }
             } else if (MODE == GM_QKV) {
                 const uint32_t half = a.head_dim >> 1;
                 for (uint32_t i = tid; 2 * i < cnt; i += NC) {
                     const uint32_t g = rb + l0 + 2 * i;
-                    const float v0 = out_tile[2 * i], v1 = out_tile[2 * i + 1];
+                    const float v0 = sm.out_tile[2 * i], v1 = sm.out_tile[2 * i + 1];
                     if (g < a.n_q + a.n_kv) {
                         const uint32_t gg = g < a.n_q ? g : g - a.n_q;
                         const uint32_t d = gg % a.head_dim;
@@ -538,41 +661,121 @@ __global__ void __launch_bounds__(MAXT, MINB) gemv_kernel(const __grid_constant_
         bar_sync(1, NC);
     }
 
+    const unsigned long long t2 = prof ? gtime_ns() : 0ull;
     if (MODE == GM_LOGITS) {
         // CTA argmax, then the last CTA to finish reduces the per-CTA results
-        // (sampler.c:28-32 semantics: the lowest index wins among equal maxima)
+        // (sampler.c:28-32: the lowest index wins among equal maxima)
 #pragma unroll
         for (int o = 16; o; o >>= 1) {
             const float ov = __shfl_xor_sync(0xffffffffu, best_v, o);
             const uint32_t oi = __shfl_xor_sync(0xffffffffu, best_i, o);
             if (ov > best_v || (ov == best_v && oi < best_i)) { best_v = ov; best_i = oi; }
         }
-        if (lane == 0) { misc[warp] = best_v; misc_u[warp] = best_i; }
+        if (lane == 0) { sm.misc[warp] = best_v; sm.misc_u[warp] = best_i; }
         bar_sync(1, NC);
         if (tid == 0) {
-            float bv = misc[0];
-            uint32_t bi = misc_u[0];
+            float bv = sm.misc[0];
+            uint32_t bi = sm.misc_u[0];
             for (uint32_t w = 1; w < NCW; ++w)
-                if (misc[w] > bv || (misc[w] == bv && misc_u[w] < bi)) { bv = misc[w]; bi = misc_u[w]; }
+                if (sm.misc[w] > bv || (sm.misc[w] == bv && sm.misc_u[w] < bi)) { bv = sm.misc[w]; bi = sm.misc_u[w]; }
             a.am_val[blockIdx.x] = bv;
             a.am_idx[blockIdx.x] = bi;
             __threadfence();
-            const uint32_t t = atomicAdd(a.ticket, 1u);
-            if (t == gridDim.x - 1) {
-                __threadfence();
-                float gv = -INFINITY;
-                uint32_t gi = 0xffffffffu;
-                for (uint32_t c = 0; c < gridDim.x; ++c) {
-                    const float cv = *(volatile float *)&a.am_val[c];
-                    const uint32_t ci = *(volatile uint32_t *)&a.am_idx[c];
-                    if (cv > gv || (cv == gv && ci < gi)) { gv = cv; gi = ci; }
+            sm.misc_u[63] = atomicAdd(a.ticket, 1u) == gridDim.x - 1 ? 1u : 0u;
+        }
+        bar_sync(1, NC);
+        if (sm.misc_u[63]) {
+            // the last CTA reduces the per-CTA results in parallel
+            __threadfence();
+            float bv = -INFINITY;
+            uint32_t bi = 0xffffffffu;
+            for (uint32_t c = tid; c < gridDim.x; c += NC) {
+                const float cv = __ldcg(&a.am_val[c]);
+                const uint32_t ci = __ldcg(&a.am_idx[c]);
+                if (cv > bv || (cv == bv && ci < bi)) { bv = cv; bi = ci; }
+            }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+            }
+            bar_sync(1, NC);
+            if (lane == 0) { sm.misc[warp] = bv; sm.misc_u[warp] = bi; }
+            bar_sync(1, NC);
+            if (tid == 0) {
+                bv = sm.misc[0];
+                bi = sm.misc_u[0];
+                for (uint32_t w = 1; w < NCW; ++w)
+                    if (sm.misc[w] > bv || (sm.misc[w] == bv && sm.misc_u[w] < bi)) { bv = sm.misc[w]; bi = sm.misc_u[w]; }
+                // every logit NaN: the reference keeps index 0
+                const uint32_t nxt = bi == 0xffffffffu ? 0u : bi;
+                *a.out_token = nxt;
+                if (a.hist) {  // feed the greedy token into the next step
+                    const uint32_t pos = __ldcg(&a.step_rw[1]);
+                    a.hist[pos] = nxt;
+                    a.step_rw[0] = nxt;
+                    a.step_rw[1] = pos + 1;
                 }
-                // all logits NaN: the reference keeps index 0
-                *a.out_token = gi == 0xffffffffu ? 0u : gi;
                 *a.ticket = 0;
             }
         }
+        bar_sync(1, NC);
     }
+    if (prof) {
+        unsigned long long *pp = a.prof + (size_t)blockIdx.x * 4;
+        pp[0] += t1 - t0;
+        pp[1] += t_wait;
+        pp[2] += t2 - t1;
+        pp[3] += gtime_ns() - t2;
+    }
+    return ok;
+}
+
+// ---------------------------------------------------------------------------
+// standalone kernel: one GEMV per launch (quant_matvec_dev and the per-kernel
+// decode path)
+// ---------------------------------------------------------------------------
+// After a failed wait: before the CTA may exit, wait (bounded) for the last
+// NS stages issued into the ring, the only copies that can be in flight.
+__device__ void ring_drain(const GemvSmem &sm, uint32_t n_issued, uint32_t NS, uint32_t *err) {
+    for (uint32_t k = n_issued > NS ? n_issued - NS : 0; k < n_issued; ++k)
+        mbar_wait(&sm.full[k % NS], (k / NS) & 1, err, ERR_WAIT_DRAIN);
+}
+
+template <int QT, bool A4>
+__global__ void __launch_bounds__(kMaxConsumers, 1) gemv_kernel(const __grid_constant__ GemvArgs a) {
+    const bool PAIRED = a.mode == GM_SWIGLU;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const GemvSmem sm = gemv_smem(smem, a.K);
+    const uint32_t tid = threadIdx.x;
+    uint32_t rb, re;
+    cta_rows(a.n_out, a.gran, rb, re);
+    const uint32_t n_st = PAIRED ? n_stages_of<true>(a, rb, re) : n_stages_of<false>(a, rb, re);
+    if (tid == 0) {
+        for (uint32_t i = 0; i < a.NS; ++i) {
+            mbar_init(&sm.full[i], 1);
+            sm.done[i] = 0;
+        }
+        fence_mbar_init();
+        // weights do not depend on the previous kernel: start streaming them
+        for (uint32_t k = 0; k < min(a.NS, n_st); ++k) {
+            if (PAIRED) issue_stage<true>(a, sm, rb, re, k, k);
+            else issue_stage<false>(a, sm, rb, re, k, k);
+        }
+    }
+    __syncthreads();
+    pdl_launch();
+    pdl_wait();  // inputs of this GEMV are outputs of the previous kernel
+    RingState rs{0, 0, 0};
+    auto refill = [&](uint32_t j, uint32_t slot) {
+        if (j + a.NS < n_st) {
+            if (PAIRED) issue_stage<true>(a, sm, rb, re, j + a.NS, slot);
+            else issue_stage<false>(a, sm, rb, re, j + a.NS, slot);
+        }
+    };
+    const bool ok = gemv_consume<QT, A4>(a, sm, tid, rs, refill);
+    if (!ok && tid == 0) ring_drain(sm, n_st, a.NS, a.err);
 }
 
 }  // namespace fwb

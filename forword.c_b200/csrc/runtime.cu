@@ -22,6 +22,7 @@
 #include "attention.cuh"
 #include "gemv.cuh"
 #include "gguf_reader.h"
+#include "decode.cuh"
 #include "misc_kernels.cuh"
 
 namespace fwb {
@@ -41,24 +42,9 @@ static void set_err(const std::string &e) { g_err = e; }
 // --------------------------------------------------------------------------
 // kernel selection
 // --------------------------------------------------------------------------
-template <int QT, int MODE, int IN>
-static const void *pick_gemv(bool a4, bool big) {
-    if (big) return a4 ? (const void *)gemv_kernel<QT, MODE, IN, true, 544, 1>
-                       : (const void *)gemv_kernel<QT, MODE, IN, false, 544, 1>;
-    return a4 ? (const void *)gemv_kernel<QT, MODE, IN, true, 288, 2>
-              : (const void *)gemv_kernel<QT, MODE, IN, false, 288, 2>;
-}
-
 template <int QT>
-static const void *pick_gemv_mode(int mode, bool a4, bool big) {
-    switch (mode) {
-    case GM_STORE: return pick_gemv<QT, GM_STORE, IN_PLAIN>(a4, big);
-    case GM_RESID: return pick_gemv<QT, GM_RESID, IN_PLAIN>(a4, big);
-    case GM_QKV: return pick_gemv<QT, GM_QKV, IN_RMSNORM>(a4, big);
-    case GM_SWIGLU: return pick_gemv<QT, GM_SWIGLU, IN_RMSNORM>(a4, big);
-    case GM_LOGITS: return pick_gemv<QT, GM_LOGITS, IN_RMSNORM>(a4, big);
-    default: return nullptr;
-    }
+static const void *pick_gemv_mode(int, bool a4, bool) {
+    return a4 ? (const void *)gemv_kernel<QT, true> : (const void *)gemv_kernel<QT, false>;
 }
 
 static const void *gemv_fn(int qt, int mode, bool a4, bool big) {
@@ -128,9 +114,8 @@ static uint32_t pow2ceil(uint32_t v) {
     return p;
 }
 
-constexpr uint32_t kStageTarget = 24 * 1024;
-constexpr uint32_t kRingBudget = 96 * 1024;
-constexpr uint32_t kMaxSmem = 227 * 1024;
+constexpr uint32_t kRingBudget = 192 * 1024;
+constexpr uint32_t kMaxSmem = 227 * 1024;  // per-block opt-in limit (static + dynamic)
 
 // Fills geometry fields of L.a (w, n_out, K, row_bytes set by the caller).
 static bool plan_gemv(int qt, int mode, int sms, GemvLaunch &L) {
@@ -138,27 +123,26 @@ static bool plan_gemv(int qt, int mode, int sms, GemvLaunch &L) {
     const uint32_t nb = a.K / 32;
     if (a.K % 32 || nb == 0 || a.n_out == 0) { set_err("gemv: bad shape"); return false; }
     const bool paired = mode == GM_SWIGLU;
+    a.mode = (uint32_t)mode;
+    a.norm = (mode == GM_QKV || mode == GM_SWIGLU || mode == GM_LOGITS) ? 1u : 0u;
     a.gran = (mode == GM_QKV || paired) ? (paired ? 1u : 2u) : 1u;
     if (mode == GM_QKV && a.n_out % 2) { set_err("gemv: odd qkv rows"); return false; }
     a.U = (nb + 1) / 2;
     a.Upad = a.U <= 32 ? std::max(8u, pow2ceil(a.U)) : (a.U + 31) / 32 * 32;
-    a.S = std::max(1u, 256u / a.Upad);
+    if (a.Upad > kMaxConsumers) { set_err("gemv: input width above 32768 is not supported"); return false; }
+    a.S = std::max(1u, kMaxConsumers / a.Upad);
     a.NC = a.S * a.Upad;
-    if (a.NC > 512) { set_err("gemv: input width above 32768 is not supported"); return false; }
-    const bool big = a.NC > 256;
+    const bool big = true;
     const uint32_t units = a.n_out / a.gran;
     const uint32_t grid = std::max(1u, std::min((uint32_t)sms, units));
     const uint32_t max_units = (units + grid - 1) / grid;
     const uint32_t max_loc = max_units * a.gran * (paired ? 2 : 1);
-    uint32_t rps = std::max(1u, kStageTarget / (a.S * a.row_bytes));
-    uint32_t R = rps * a.S;
-    const bool need_even = paired || mode == GM_QKV;
-    if (need_even && (R & 1)) R *= 2;
-    const uint32_t cap = (max_loc + a.S - 1) / a.S * a.S;
-    if (R > cap) {
-        R = cap;
-        if (need_even && (R & 1)) R += a.S;
+    if ((paired || mode == GM_QKV) && (rows_per_thread(qt) * a.S) % 2) {  // whole pairs per stage
+        if (a.S == 1) { set_err("gemv: odd stage rows for a pair mode"); return false; }
+        a.S &= ~1u;
+        a.NC = a.S * a.Upad;
     }
+    const uint32_t R = rows_per_thread(qt) * a.S;  // rows per round = per ring stage
     a.R = R;
     uint32_t stage;
     if (paired) {
@@ -169,17 +153,19 @@ static bool plan_gemv(int qt, int mode, int sms, GemvLaunch &L) {
     }
     a.stage_bytes = stage;
     const uint32_t n_st = (max_loc + R - 1) / R;
-    uint32_t ns = std::max(2u, std::min((uint32_t)kMaxStages, kRingBudget / stage));
+    uint32_t ns = std::max(2u, std::min((uint32_t)kMaxStages, (kRingBudget - plane_bytes(a.K)) / stage));
     ns = std::max(1u, std::min(ns, n_st));
-    while (ns > 1 && kHeaderBytes + ns * stage + 128 > kMaxSmem) --ns;
-    if (kHeaderBytes + ns * stage + 128 > kMaxSmem) { set_err("gemv: stage does not fit shared memory"); return false; }
+    if (const char *e = getenv("FWB_MAX_NS")) ns = std::max(1u, std::min(ns, (uint32_t)atoi(e)));
+    const uint32_t room = kMaxSmem - 1024 - plane_bytes(a.K);  // static shared memory stays below 1 KB
+    while (ns > 1 && kHeaderBytes + ns * stage + 128 > room) --ns;
+    if (kHeaderBytes + ns * stage + 128 > room) { set_err("gemv: stage does not fit shared memory"); return false; }
     a.NS = ns;
     const bool a4 = (nb % 2 == 0) && ((uintptr_t)a.w % 4 == 0) && (!a.w2 || (uintptr_t)a.w2 % 4 == 0);
     L.fn = gemv_fn(qt, mode, a4, big);
     if (!L.fn) { set_err("gemv: unsupported quant type"); return false; }
     L.grid = dim3(grid);
-    L.block = dim3(a.NC + 32);
-    L.smem = kHeaderBytes + (size_t)ns * stage + 128;
+    L.block = dim3(a.NC);
+    L.smem = kHeaderBytes + plane_bytes(a.K) + (size_t)ns * stage + 128;
     L.weight_bytes = (uint64_t)a.n_out * a.row_bytes * (paired ? 2 : 1);
     return true;
 }
@@ -192,9 +178,12 @@ static bool set_smem_attrs(int dev) {
     for (int qt : qts)
         for (int mode = 0; mode <= GM_LOGITS; ++mode)
             for (int a4 = 0; a4 < 2; ++a4)
-                for (int big = 0; big < 2; ++big) {
+                for (int big = 0; big < 1; ++big) {
                     const void *fn = gemv_fn(qt, mode, a4, big);
-                    CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem));
+                    cudaFuncAttributes fa;
+                    CK(cudaFuncGetAttributes(&fa, fn));
+                    const int dyn = (int)kMaxSmem - (int)fa.sharedSizeBytes;
+                    CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn));
                 }
     g_attr_done[dev] = true;
     return true;
@@ -246,6 +235,7 @@ static bool matvec_dev(const void *w, size_t w_size, uint32_t type, const float 
     uint32_t bb, row_bytes;
     if (!matvec_args_ok(w, w_size, type, x, y, in, out, bb, row_bytes)) return false;
     if ((uintptr_t)w % 2) { set_err("quant_matvec_dev: weights must be 2-byte aligned"); return false; }
+    if ((uintptr_t)x % 16) { set_err("quant_matvec_dev: input must be 16-byte aligned"); return false; }
     int dev;
     CK(cudaGetDevice(&dev));
     if (!set_smem_attrs(dev)) return false;
@@ -281,6 +271,7 @@ struct Step {
     std::string name;
     std::function<cudaError_t(cudaStream_t, bool)> run;
     uint64_t bytes = 0;  // algorithmic HBM bytes of this launch
+    Phase phase{};       // the same work as a phase of the persistent kernel
 };
 
 }  // namespace fwb
@@ -308,6 +299,11 @@ struct fwb_model {
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     bool use_graph = true, use_pdl = true;
+    bool persistent = true;          // one persistent kernel per token (else one kernel per phase)
+    unsigned long long *prof = nullptr;  // [n_phases][G][4] GEMV profile (FWB_TRACE=1)
+    fwb::DecodeArgs dargs{};
+    size_t dsmem = 0;
+    uint32_t *sync = nullptr;
     std::vector<void *> allocs;
 };
 
@@ -361,6 +357,7 @@ static bool upload(const uint8_t *src, uint8_t *dst, uint64_t bytes, uint8_t *st
 }
 
 static bool build_steps(fwb_model *m);
+static bool build_decode(fwb_model *m);
 
 static bool load_model(fwb_model *m, const char *path, size_t max_ctx) {
     std::string err;
@@ -375,7 +372,7 @@ static bool load_model(fwb_model *m, const char *path, size_t max_ctx) {
     if (c.n_head % c.n_head_kv) { set_err("attention: invalid head configuration"); return false; }
     const uint32_t E = c.n_embd, F = c.n_ff, hd = c.head_dim, H = c.n_head, KV = c.n_head_kv;
     if (!attn_fn(hd, H / KV)) { set_err("head_dim / GQA group outside this build"); return false; }
-    if (E % 64 || F % 64 || (H * hd) != E) { set_err("model widths outside this build"); return false; }
+    if (E % 32 || F % 32 || (H * hd) != E) { set_err("model widths outside this build"); return false; }
 
     // resolve tensors once
     const GgufTensor *te = m->gguf.find("token_embd.weight");
@@ -538,17 +535,6 @@ static uint32_t attn_splits(const fwb_model *m) {
     return std::max(1u, s);
 }
 
-// Feeds the greedy token of this step into the next one: step[0] = next
-// token, step[1] = pos + 1, hist[pos] = next token.
-__global__ void fwb_advance_kernel(uint32_t *step, uint32_t *hist) {
-    if (threadIdx.x == 0) {
-        const uint32_t nxt = step[2], pos = step[1];
-        hist[pos] = nxt;
-        step[0] = nxt;
-        step[1] = pos + 1;
-    }
-}
-
 static bool build_steps(fwb_model *m) {
     const ModelConfig &c = m->cfg;
     const uint32_t E = c.n_embd, F = c.n_ff, hd = c.head_dim, H = c.n_head, KV = c.n_head_kv;
@@ -563,6 +549,8 @@ static bool build_steps(fwb_model *m) {
         uint32_t *step = m->step;
         float *x = m->x;
         s.bytes = rb;
+        s.phase.kind = PH_EMBED;
+        s.phase.e = EmbedArgs{e.p, e.type, e.cols, rb, step, x};
         s.run = [=](cudaStream_t st, bool pdl) {
             const uint8_t *p = e.p;
             uint32_t t = e.type, cols = e.cols;
@@ -595,6 +583,11 @@ static bool build_steps(fwb_model *m) {
         Step s;
         s.name = name;
         s.bytes = L.weight_bytes;
+        s.phase.kind = PH_GEMV;
+        s.phase.qt = w.type;
+        s.phase.mode = (uint32_t)mode;
+        s.phase.a4 = (w.cols / 32) % 2 == 0 && (uintptr_t)w.p % 4 == 0 && (!w2 || (uintptr_t)w2->p % 4 == 0);
+        s.phase.g = L.a;
         s.run = [L](cudaStream_t st, bool pdl) {
             GemvArgs a = L.a;
             void *args[] = {&a};
@@ -640,6 +633,13 @@ static bool build_steps(fwb_model *m) {
             a.step = m->step;
             a.err = m->err;
             s.bytes = 0;  // KV bytes depend on pos; accounted separately
+            a.n_kv = KV;
+            s.phase.kind = PH_ATTN;
+            s.phase.hd = hd;
+            s.phase.gq = H / KV;
+            s.phase.at = a;
+            // the persistent kernel runs one (KV head, split) item per CTA
+            s.phase.at.n_split = std::max(1u, std::min(nsplit, (uint32_t)m->sms / KV));
             s.run = [a, afn, KV, nsplit](cudaStream_t st, bool pdl) {
                 AttnArgs aa = a;
                 void *args[] = {&aa};
@@ -658,28 +658,137 @@ static bool build_steps(fwb_model *m) {
         ex.am_idx = m->am_idx;
         ex.ticket = m->am_ticket;
         ex.out_token = m->step + 2;
+        ex.step_rw = m->step;
+        ex.hist = m->hist;
         if (!gemv_step("lm_head_argmax", GM_LOGITS, m->head, nullptr, c.n_vocab, m->x, m->out_norm, m->logits, ex))
             return false;
     }
     // The head GEMV needs a norm weight; a model without output_norm gets the
     // identity norm (transformer.c:355-357 copies x unnormalised): not supported.
     if (!m->out_norm) { set_err("output_norm.weight is required by this build"); return false; }
-    {  // advance: step[0] = next token, step[1] = pos + 1, hist[pos] = next
-        Step s;
-        s.name = "advance";
-        uint32_t *step = m->step, *hist = m->hist;
-        s.run = [step, hist](cudaStream_t st, bool pdl) {
-            (void)pdl;
-            uint32_t *a0 = step, *a1 = hist;
-            void *args[] = {&a0, &a1};
-            return launch_ex((const void *)fwb_advance_kernel, dim3(1), dim3(32), 0, st, args, false);
-        };
-        m->steps.push_back(std::move(s));
+    return !m->persistent || build_decode(m);
+}
+
+// Phases of the persistent kernel: the Step list's work, with one ring
+// geometry for all GEMV phases and per-CTA weight-stream tables.
+static bool build_decode(fwb_model *m) {
+    const uint32_t G = (uint32_t)m->sms;
+    std::vector<Phase> ph;
+    for (const Step &s : m->steps) ph.push_back(s.phase);
+    const uint32_t n_ph = (uint32_t)ph.size();
+    uint32_t stage = 0, scratch = 0;
+    for (const Phase &p : ph) {
+        if (p.kind == PH_GEMV) {
+            stage = std::max(stage, p.g.stage_bytes);
+            scratch = std::max(scratch, plane_bytes(p.g.K));
+        }
     }
+    {  // attention scratch of the persistent kernel (16 warps)
+        const uint32_t hd = m->cfg.head_dim, gq = m->cfg.n_head / m->cfg.n_head_kv;
+        const uint32_t nw = kDecodeThreads / 32;
+        const uint32_t att = (nw * 32 + 2 * nw * gq + nw * gq * hd + kMaxSplits * gq + gq + 1) * 4;
+        scratch = std::max(scratch, (att + 127) / 128 * 128);
+    }
+    cudaFuncAttributes fa;
+    CK(cudaFuncGetAttributes(&fa, (const void *)decode_kernel));
+    const size_t tab_bytes = (size_t)n_ph * sizeof(StageSrc);
+    const size_t fixed = kHeaderBytes + scratch + 128 + tab_bytes + fa.sharedSizeBytes + 1024;
+    if (fixed + 2 * (size_t)stage > kMaxSmem) { set_err("persistent kernel: shared memory too small"); return false; }
+    uint32_t ns = (uint32_t)std::min<size_t>(kMaxStages, (kMaxSmem - fixed) / stage);
+    if (const char *e = getenv("FWB_MAX_NS")) ns = std::max(2u, std::min(ns, (uint32_t)atoi(e)));
+    const char *trc = getenv("FWB_TRACE");
+    const bool tracing = trc && *trc == '1';
+    if (tracing && !dalloc(m, (void **)&m->prof, (size_t)n_ph * G * 4 * 8)) return false;
+    for (uint32_t i = 0; i < n_ph; ++i) {
+        Phase &p = ph[i];
+        if (p.kind == PH_GEMV) {
+            p.g.NS = ns;
+            p.g.stage_bytes = stage;
+            p.g.prof = tracing ? m->prof + (size_t)i * G * 4 : nullptr;
+        }
+    }
+    // per-CTA stream tables
+    std::vector<StageSrc> tab((size_t)G * n_ph);
+    std::vector<uint32_t> nst(G, 0);
+    for (uint32_t c = 0; c < G; ++c) {
+        uint32_t first = 0;
+        for (uint32_t p = 0; p < n_ph; ++p) {
+            StageSrc &t = tab[(size_t)c * n_ph + p];
+            t = StageSrc{};
+            t.first = first;
+            if (ph[p].kind != PH_GEMV) continue;
+            const GemvArgs &g = ph[p].g;
+            const uint32_t n = g.n_out / g.gran;
+            const uint32_t b = (uint32_t)((uint64_t)c * n / G) * g.gran, e = (uint32_t)((uint64_t)(c + 1) * n / G) * g.gran;
+            const bool paired = ph[p].mode == GM_SWIGLU;
+            t.a = (uint64_t)(uintptr_t)g.w + (uint64_t)b * g.row_bytes;
+            t.b = paired ? (uint64_t)(uintptr_t)g.w2 + (uint64_t)b * g.row_bytes : 0;
+            t.rows = e - b;
+            t.row_bytes = g.row_bytes;
+            t.R = g.R;
+            t.paired = paired;
+            const uint32_t n_loc = paired ? 2 * (e - b) : (e - b);
+            t.n_st = (n_loc + g.R - 1) / g.R;
+            first += t.n_st;
+        }
+        nst[c] = first;
+    }
+    Phase *d_ph;
+    StageSrc *d_tab;
+    uint32_t *d_nst;
+    if (!dalloc(m, (void **)&d_ph, ph.size() * sizeof(Phase)) || !dalloc(m, (void **)&d_tab, tab.size() * sizeof(StageSrc)) ||
+        !dalloc(m, (void **)&d_nst, G * 4) || !dalloc(m, (void **)&m->sync, 64))
+        return false;
+    CK(cudaMemcpy(d_ph, ph.data(), ph.size() * sizeof(Phase), cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(d_tab, tab.data(), tab.size() * sizeof(StageSrc), cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(d_nst, nst.data(), G * 4, cudaMemcpyHostToDevice));
+    DecodeArgs &d = m->dargs;
+    d.ph = d_ph;
+    d.src = d_tab;
+    d.n_ph = n_ph;
+    d.total_st = *std::max_element(nst.begin(), nst.end());
+    d.NS = ns;
+    d.stage_bytes = stage;
+    d.scratch_bytes = scratch;
+    d.sync = m->sync;
+    d.err = m->err;
+    d.n_st_cta = d_nst;
+    const char *tr = getenv("FWB_TRACE");
+    if (tr && *tr == '1') {
+        if (!dalloc(m, (void **)&d.trace, (2 * n_ph + 1) * 8)) return false;
+    }
+    m->dsmem = kHeaderBytes + scratch + (size_t)ns * stage + 128 + tab_bytes;
+    CK(cudaFuncSetAttribute((const void *)decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->dsmem));
+    int per_sm = 0;
+    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, (const void *)decode_kernel, kDecodeThreads, m->dsmem));
+    if (per_sm < 1) { set_err("persistent kernel does not fit on an SM"); return false; }
     return true;
 }
 
+static cudaError_t launch_decode(fwb_model *m) {
+    cudaError_t e = cudaMemsetAsync(m->sync, 0, 8, m->st);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(m->sms);
+    cfg.blockDim = dim3(kDecodeThreads);
+    cfg.dynamicSmemBytes = m->dsmem;
+    cfg.stream = m->st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeCooperative;
+    at[0].val.cooperative = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    DecodeArgs d = m->dargs;
+    void *args[] = {&d};
+    return cudaLaunchKernelExC(&cfg, (const void *)decode_kernel, args);
+}
+
 static bool run_steps(fwb_model *m) {
+    if (m->persistent) {
+        cudaError_t e = launch_decode(m);
+        if (e != cudaSuccess) { set_err(std::string("persistent decode launch: ") + cudaGetErrorString(e)); return false; }
+        return true;
+    }
     for (size_t i = 0; i < m->steps.size(); ++i) {
         cudaError_t e = m->steps[i].run(m->st, m->use_pdl && i > 0);
         if (e != cudaSuccess) {
@@ -815,6 +924,8 @@ fwb_model_t *fwb_model_open(const char *path, size_t max_ctx, int device) {
     const char *np = getenv("FWB_NO_PDL");
     m->use_graph = !(ng && *ng == '1');
     m->use_pdl = !(np && *np == '1');
+    const char *mk = getenv("FWB_KERNEL_PER_PHASE");
+    m->persistent = !(mk && *mk == '1');
     if (cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking) != cudaSuccess || !set_smem_attrs(device) ||
         !load_model(m, path, max_ctx) || (m->use_graph && !capture_graph(m))) {
         std::string e = g_err;
@@ -919,6 +1030,28 @@ int fwb_kv_read(fwb_model_t *m, size_t layer, size_t pos0, size_t n, float *k, f
 }
 
 const float *fwb_logits_dev(fwb_model_t *m) { return m ? m->logits : nullptr; }
+
+int fwb_prof_read(fwb_model_t *m, uint64_t *out, size_t n) {
+    if (!m || !m->prof) { set_err("profiling is off (set FWB_TRACE=1 before opening)"); return -1; }
+    const size_t cnt = (size_t)m->dargs.n_ph * m->sms * 4;
+    if (n < cnt) { set_err("profile buffer too small"); return -1; }
+    cudaSetDevice(m->dev);
+    if (cudaMemcpy(out, m->prof, cnt * 8, cudaMemcpyDeviceToHost) != cudaSuccess) { set_err("profile copy"); return -1; }
+    cudaMemset(m->prof, 0, cnt * 8);
+    return (int)cnt;
+}
+
+int fwb_trace_read(fwb_model_t *m, uint64_t *out, size_t n, char *names, size_t name_stride) {
+    if (!m || !m->persistent || !m->dargs.trace) { set_err("tracing is off (set FWB_TRACE=1 before opening)"); return -1; }
+    const size_t np = 2 * (size_t)m->dargs.n_ph + 1;
+    if (n < np) { set_err("trace buffer too small"); return -1; }
+    cudaSetDevice(m->dev);
+    if (cudaMemcpy(out, m->dargs.trace, np * 8, cudaMemcpyDeviceToHost) != cudaSuccess) { set_err("trace copy"); return -1; }
+    if (names)
+        for (size_t i = 0; i < m->steps.size(); ++i)
+            snprintf(names + i * name_stride, name_stride, "%s", m->steps[i].name.c_str());
+    return (int)np;
+}
 void *fwb_stream(fwb_model_t *m) { return m ? (void *)m->st : nullptr; }
 
 }  // extern "C"

@@ -125,6 +125,24 @@ int fwb_kv_load(fwb_model_t *m, size_t layer, size_t pos0, size_t n, const float
                 const float *v);
 int fwb_kv_read(fwb_model_t *m, size_t layer, size_t pos0, size_t n, float *k, float *v);
 
+/*
+ * Phase timeline of the last decode step of the persistent kernel (tracing
+ * aid; open the model with FWB_TRACE=1 in the environment).  GPU global timer
+ * (ns) seen by CTA 0: out[2i] at the start of phase i, out[2i+1] when it
+ * reaches the barrier after phase i, out[2*n_phases] at the end.  names
+ * (optional) gets one NUL-terminated phase name per name_stride bytes.
+ * Returns 2*n_phases + 1, or -1.
+ */
+int fwb_trace_read(fwb_model_t *m, uint64_t *out, size_t n, char *names, size_t name_stride);
+
+/*
+ * Accumulated GEMV profile of the persistent kernel since the last read
+ * (FWB_TRACE=1): out[(phase * n_sm + cta) * 4 + i] = ns that CTA spent in
+ * i = 0 input prologue, 1 waiting for weight stages, 2 row loop, 3 tail.
+ * Resets the counters.  Returns the number of values written, or -1.
+ */
+int fwb_prof_read(fwb_model_t *m, uint64_t *out, size_t n);
+
 /* Device logits of the last step (n_vocab fp32) and the model's CUDA stream. */
 const float *fwb_logits_dev(fwb_model_t *m);
 void *fwb_stream(fwb_model_t *m);
