@@ -1,0 +1,412 @@
+#!/usr/bin/env python3
+"""Batch-1 decode benchmark of forword.c's per-token forward on B200.
+
+Workload (N=1): the Llama-3-8B-shaped decoder with every linear weight in
+GGUF Q4_0 (embedding and norms fp32), random-init N(0, 0.02) from a seed and
+written as a GGUF file.  A 512-token uniform-random prompt is fed through the
+per-token forward (the reference's own prompt loop, main.c:145-151), then
+greedy decode runs at batch 1: W untimed warm-up tokens, then K timed tokens.
+One step = one token = one `transformer_forward` (one launch of the
+persistent decode kernel).
+
+Arms
+  --impl b200       (default) the CUDA library through its C ABI
+                    (include/forword_b200.h):
+                    value  device-timed greedy decode, the token chosen on the
+                           device feeds the next step; weights resident in HBM.
+                    e2e    `fwb_forward` per token with host buffers: token/pos
+                           copied in, the full logits row copied out to pinned
+                           host memory, the next token picked on the host
+                           (sampler_argmax, sampler.c:28-32) — what the
+                           reference's main loop does with transformer_forward.
+  --impl reference  the reference's own CPU decode step (its sources compiled
+                    by oracle/Makefile into oracle/_ref, else the oracle's C
+                    restatement), same model and positions, timed on the host.
+
+Multi-GPU (--gpus N under torchrun): every rank decodes its own replica of the
+8B model; there is no exchange between ranks, so the line reports
+"scaling": "weak" and value = all ranks' tokens / the slowest rank's time.
+
+Every weight byte of a step is streamed from HBM (4.2 GB per token against a
+126 MB L2), so no explicit L2 flush is needed between steps.
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import datetime
+import io
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "forword.c_b200"))
+
+import numpy as np  # noqa: E402
+
+from fwb import configs, gguf_synth  # noqa: E402
+
+METRIC = "batch-1 decode tokens/s per box"
+UNIT = "tokens/s"
+PROMPT = 512
+MODEL_SEED = 1
+PROMPT_SEED = 2024
+CFG = configs.LLAMA8B_Q4_0
+WORKLOAD = ("llama-3-8B-shaped decoder, all linear weights Q4_0, fp32 embedding/norms, "
+            "random-init N(0,0.02); 512-token random prompt fed per token, then greedy "
+            "decode at batch 1")
+
+
+def _args():
+    p = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=256, help="timed decode tokens per rank")
+    p.add_argument("--warmup", type=int, default=8, help="untimed decode tokens before timing")
+    p.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    p.add_argument("--no-cpu-baseline", action="store_true",
+                   help="skip the timed reference sample in the b200 arm")
+    p.add_argument("--cpu-budget-s", type=float, default=15.0,
+                   help="CPU seconds for the reference sample inside the b200 arm")
+    p.add_argument("--ref-budget-s", type=float, default=150.0,
+                   help="cap on the timed CPU seconds of the --impl reference arm")
+    p.add_argument("--model-dir", default=None, help="where the synthetic GGUF is cached")
+    return p.parse_args()
+
+
+def _peaks() -> tuple[float, str]:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def _dist():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return rank, world, local
+
+
+def _model_path(args) -> str:
+    return gguf_synth.cached_model(CFG, seed=MODEL_SEED, directory=args.model_dir)
+
+
+def _prompt() -> np.ndarray:
+    return np.random.default_rng(PROMPT_SEED).integers(0, CFG.n_vocab, PROMPT).astype(np.uint32)
+
+
+def _kv_bytes_per_position() -> int:
+    return 2 * CFG.n_layer * CFG.n_head_kv * CFG.head_dim * 4
+
+
+def _config(world: int, k_steps: int, w_steps: int, kv_ctx: int) -> dict:
+    return {
+        "workload": WORKLOAD,
+        "model": CFG.name,
+        "global_batch": 1,
+        "prompt_tokens": PROMPT,
+        "decode_positions": [PROMPT + w_steps, PROMPT + w_steps + k_steps],
+        "kv_ctx": kv_ctx,
+        "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+        "l2": "inputs larger than L2: every step streams the 4.2 GB of quantised weights",
+    }
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+_CLOCK_FIELDS = ("timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+
+class ClockSampler:
+    """nvidia-smi sampled every 100 ms for one device (read-only queries)."""
+
+    def __init__(self, device: int):
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(device), f"--query-gpu={_CLOCK_FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        self.t0 = self.t1 = None
+
+    def mark_start(self):
+        self.t0 = datetime.datetime.now()
+
+    def mark_end(self):
+        self.t1 = datetime.datetime.now()
+
+    def finish(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = []
+        for r in csv.reader(io.StringIO(out)):
+            if len(r) < 9:
+                continue
+            r = [c.strip() for c in r]
+            try:
+                ts = datetime.datetime.strptime(r[0], "%Y/%m/%d %H:%M:%S.%f")
+                rows.append((ts, float(r[1]), float(r[2]), r[5:9]))
+            except ValueError:
+                continue
+        inside = [x for x in rows if self.t0 and self.t1 and self.t0 <= x[0] <= self.t1]
+        use = inside or rows
+        if not use:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({names[i] for x in use for i, v in enumerate(x[3]) if v == "Active"})
+        return {"sm_mhz": statistics.median(x[1] for x in use), "sm_max_mhz": max(x[2] for x in use),
+                "reasons": reasons, "samples": len(use),
+                "window": "timed region" if inside else "whole run (no sample inside the timed region)"}
+
+
+# ---------------------------------------------------------------------------
+# reference CPU step (the baseline; never the product path)
+# ---------------------------------------------------------------------------
+def _reference_model(path: str, kv_ctx: int):
+    """The reference decode step on the host: compiled reference when built, else the port."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import pyoracle
+    if pyoracle.ref_available():
+        return pyoracle.RefModel(path, max_ctx=kv_ctx), "reference"
+    return pyoracle.OracleModel(path, max_ctx=kv_ctx), "port"
+
+
+def _time_reference(path: str, n_max: int, budget_s: float, warm: int = 1):
+    """Decode steps of the reference at positions PROMPT.. after a K/V pre-fill.
+
+    The prompt's K/V rows are written directly (N(0,1) values) instead of
+    running 512 prompt steps on the CPU (≈1 h for this model); each timed step
+    then does the same weight streaming and the same 512+ position attention as
+    a real decode step.  Returns (tokens/s, steps timed, kind, seconds).
+    """
+    n_max = max(1, min(n_max, 512))
+    ref, kind = _reference_model(path, PROMPT + warm + n_max + 1)
+    rng = np.random.default_rng(7)
+    for layer in range(CFG.n_layer):
+        k = rng.standard_normal((PROMPT, CFG.n_head_kv, CFG.head_dim), dtype=np.float32)
+        v = rng.standard_normal((PROMPT, CFG.n_head_kv, CFG.head_dim), dtype=np.float32)
+        ref.kv_load(layer, 0, k, v)
+    tok, pos = int(_prompt()[-1]), PROMPT
+    for _ in range(warm):
+        tok = int(np.argmax(ref.forward(tok, pos)))
+        pos += 1
+    n, t0 = 0, time.perf_counter()
+    while n < n_max:
+        tok = int(np.argmax(ref.forward(tok, pos)))
+        pos += 1
+        n += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = time.perf_counter() - t0
+    ref.close()
+    return n / dt, n, kind, dt
+
+
+def run_reference(args) -> None:
+    rank, world, _ = _dist()
+    if rank != 0:
+        return
+    path = _model_path(args)
+    tps, n, kind, dt = _time_reference(path, args.steps, args.ref_budget_s, warm=1)
+    sample = (f"{n} greedy decode steps of the 8B Q4_0 model at positions {PROMPT + 1}..{PROMPT + n} "
+              f"after a 512-position K/V pre-fill (1 untimed warm-up step; {args.steps} requested, "
+              f"capped at {args.ref_budget_s:.0f} s)")
+    line = {
+        "metric": METRIC, "value": tps, "unit": UNIT, "n_gpus": args.gpus, "steps": n,
+        "warmup": 1, "ms_per_step": dt / n * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded random weights and prompt)",
+        "config": _config(1, n, 1, PROMPT + n + 2), "impl": "reference",
+        "cpu_baseline": {"value": tps, "unit": UNIT, "cores": 1, "kind": kind, "sample": sample,
+                         "host_cores": os.cpu_count(),
+                         "note": "the reference decode step is single-threaded by design"},
+        "e2e": {"value": tps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# the B200 arm
+# ---------------------------------------------------------------------------
+def run_b200(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from fwb.model import Model
+
+    rank, world, local = _dist()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900),
+                                device_id=torch.device(f"cuda:{local}"))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    if rank == 0:
+        path = _model_path(args)
+    barrier()
+    if rank != 0:
+        path = _model_path(args)
+
+    K, W = args.steps, args.warmup
+    if K < 1 or W < 0:
+        raise SystemExit("--steps must be >= 1 and --warmup >= 0")
+    need = PROMPT + 2 * (W + K) + 1
+    kv_ctx = max(1024, 1 << (need - 1).bit_length())
+    if kv_ctx > CFG.n_ctx:
+        raise SystemExit(f"--steps/--warmup need {need} positions > n_ctx {CFG.n_ctx}")
+
+    m = Model(path, max_ctx=kv_ctx, device=local)
+    stream = torch.cuda.ExternalStream(m.stream, device=torch.device(f"cuda:{local}"))
+
+    # prompt: one forward per token (teacher forced), as the reference's main loop
+    prompt = _prompt()
+    tok = 0
+    for i, t in enumerate(prompt):
+        tok = m.forward_argmax(int(t), i)
+    pos = PROMPT
+
+    # warm-up
+    if W:
+        toks = m.generate_greedy(tok, pos, W)
+        tok, pos = int(toks[-1]), pos + W
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler(local) if rank == 0 else None
+    if clocks:
+        time.sleep(1.0)  # let nvidia-smi start sampling
+
+    # ---- device-timed greedy decode: K steps, weights resident in HBM ----
+    pos_timed = pos
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    if clocks:
+        clocks.mark_start()
+    e0.record(stream)
+    toks = m.generate_greedy(tok, pos, K)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if clocks:
+        clocks.mark_end()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    tok, pos = int(toks[-1]), pos + K
+
+    # ---- end to end through fwb_forward with host buffers ----
+    logits = torch.empty(m.n_vocab, dtype=torch.float32, pin_memory=True).numpy()
+    for _ in range(min(W, 3)):  # first use of the pinned logits path
+        m.forward(tok, pos, out=logits)
+        tok, pos = int(np.argmax(logits)), pos + 1
+    barrier()
+    torch.cuda.synchronize()
+    f0 = torch.cuda.Event(enable_timing=True)
+    f1 = torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(K):
+        m.forward(tok, pos, out=logits)
+        tok, pos = int(np.argmax(logits)), pos + 1
+    f1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms_e2e = max_over_ranks(f0.elapsed_time(f1))
+
+    kernels = m.kernels_per_step
+    weight_bytes = m.weight_bytes
+    m.close()
+    clk = clocks.finish() if clocks else None
+
+    if rank == 0:
+        peak, peak_kind = _peaks()
+        # algorithmic bytes of one decode-kernel launch at position p: every
+        # weight byte once, the K/V rows 0..p once, the new K/V row, the logits
+        kvp = _kv_bytes_per_position()
+        mean_pos = pos_timed + (K - 1) / 2.0
+        step_bytes = weight_bytes + kvp * (mean_pos + 1) + kvp + 4 * CFG.n_vocab
+        launch_s = ms / 1e3 / K
+        achieved = step_bytes / launch_s / 1e9
+        line = {
+            "metric": METRIC, "value": world * K / (ms / 1e3), "unit": UNIT, "n_gpus": world,
+            "steps": K, "warmup": W, "ms_per_step": ms / K, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "q4_0 weights x 16-bit block fixed-point activations (dp4a), fp32 accumulate",
+            "data": "synthetic (seeded random weights and prompt)",
+            "config": _config(world, K, W, kv_ctx),
+            "roofline": {
+                "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "peak_source": f"hbm_gbs ({peak_kind})",
+                "traffic": _ncu_traffic(),
+                "kernel": "decode_kernel (persistent, one launch per token)",
+                "bytes_per_launch": step_bytes,
+                "frac_weights_only": weight_bytes / launch_s / 1e9 / peak,
+                "launch_time": "events over the K timed launches / K (includes the 8-byte "
+                               "step-counter memset node of each graph)",
+            },
+            "e2e": {"value": world * K / (ms_e2e / 1e3), "unit": UNIT,
+                    "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4 * CFG.n_vocab + 8,
+                    "api": "fwb_forward (transformer_forward) with pinned host logits, host argmax"},
+            "clocks": clk,
+            "gpu_launches": kernels * K,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            tps, n, kind, dt = _time_reference(path, 1 << 30, args.cpu_budget_s, warm=1)
+            line["cpu_baseline"] = {
+                "value": tps, "unit": UNIT, "cores": 1, "kind": kind, "host_cores": os.cpu_count(),
+                "sample": f"{n} greedy decode steps of the same model at positions "
+                          f"{PROMPT + 1}..{PROMPT + n} after a 512-position K/V pre-fill "
+                          f"({dt:.1f} s)"}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def _ncu_traffic():
+    """DRAM bytes per decode-kernel launch from the committed ncu summary, if any."""
+    p = os.path.join(ROOT, "profiles", "decode_kernel_8b_q4_0.md")
+    try:
+        with open(p) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch:"):
+                    return float(line.split(":", 1)[1])
+    except OSError:
+        pass
+    return None
+
+
+def main() -> None:
+    args = _args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

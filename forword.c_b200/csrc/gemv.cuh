@@ -8,11 +8,14 @@
 // output rows, so its weights are one contiguous byte range of the GGUF
 // tensor (the bytes are used in their GGUF layout, never repacked).
 //
-// Data movement.  A producer warp streams that range through a ring of
-// shared-memory stages with 1-D bulk async copies (cp.async.bulk, no
-// multicast) completing on mbarriers; it starts before griddepcontrol.wait,
-// so under programmatic dependent launch the weights of this GEMV stream in
-// while the previous kernel of the decode step is still running.
+// Data movement.  The range streams through a ring of shared-memory stages
+// with 1-D bulk async copies (cp.async.bulk, no multicast) completing on
+// mbarriers.  There is no producer warp: all 16 warps compute, and the last
+// warp to finish with a stage (a shared-memory counter per stage) issues the
+// copy that refills it.  The first NS stages are issued before
+// griddepcontrol.wait, so under programmatic dependent launch the weights of
+// this GEMV stream in while the previous kernel is still running (in the
+// persistent decode kernel the ring runs on across phases instead).
 //
 // Arithmetic.  Consumer thread (slot s, unit u) owns columns [64u, 64u+64)
 // of RPT rows per round (independent instruction streams).  Its 64 inputs are

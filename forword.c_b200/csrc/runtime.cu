@@ -952,6 +952,11 @@ int fwb_model_dims(const fwb_model_t *m, uint32_t *d) {
 
 uint64_t fwb_model_weight_bytes(const fwb_model_t *m) { return m ? m->weight_bytes : 0; }
 
+int fwb_model_kernels_per_step(const fwb_model_t *m) {
+    if (!m) return -1;
+    return m->persistent ? 1 : (int)m->steps.size();
+}
+
 int fwb_forward(fwb_model_t *m, uint32_t token, size_t pos, float *logits_host) {
     if (!m) return -1;
     cudaSetDevice(m->dev);

@@ -56,6 +56,10 @@ class Model:
         return int(self.lib.fwb_model_weight_bytes(self.h))
 
     @property
+    def kernels_per_step(self) -> int:
+        return int(self.lib.fwb_model_kernels_per_step(self.h))
+
+    @property
     def stream(self) -> int:
         return int(self.lib.fwb_stream(self.h) or 0)
 

@@ -80,3 +80,4 @@ def _declare(lib) -> None:
     sig("fwb_trace_read", _i32, _vp, _c.POINTER(_u64), _sz, _c.c_char_p, _sz)
     sig("fwb_prof_read", _i32, _vp, _c.POINTER(_u64), _sz)
     sig("fwb_model_weight_bytes", _u64, _vp)
+    sig("fwb_model_kernels_per_step", _i32, _vp)

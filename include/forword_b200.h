@@ -96,6 +96,10 @@ int fwb_model_dims(const fwb_model_t *m, uint32_t *dims);
 /* Quantised bytes one decode step streams (weights + norms + one embedding row). */
 uint64_t fwb_model_weight_bytes(const fwb_model_t *m);
 
+/* Kernels one decode step launches: 1 for the persistent decode kernel
+ * (default), one per phase with FWB_KERNEL_PER_PHASE=1.  -1 for NULL. */
+int fwb_model_kernels_per_step(const fwb_model_t *m);
+
 /*
  * transformer_forward (transformer.c:149-326): feed token_id at position pos
  * and write n_vocab fp32 logits to logits_host (host memory; may be NULL to
