@@ -255,6 +255,90 @@ static bool matvec_dev(const void *w, size_t w_size, uint32_t type, const float 
 }
 
 // --------------------------------------------------------------------------
+// quant_matvec_static: quant_matvec staged through one fixed device array
+// instead of per-call allocations
+// --------------------------------------------------------------------------
+// Layout of the array for one call (byte offsets):
+//   [0, 256)       the GEMV kernel's error word (uint32 at 0).  The only part
+//                  that must be zero when the kernel starts; zeroed before
+//                  every launch.
+//   kStaticX       input vector, fp32
+//   off_w          weight rows, 256-aligned with 256 bytes of slack on both
+//                  sides (the kernel's 16-byte bulk copies read up to 15
+//                  bytes outside the rows)
+//   off_y          output vector, fp32
+constexpr size_t kStaticScratchBytes = size_t(32) << 20;
+constexpr size_t kStaticX = 256;
+static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
+static uint8_t *g_static_base[64];  // device address of g_static_scratch, per device
+
+static size_t round256(size_t v) { return (v + 255) & ~size_t(255); }
+
+// Set-up on the first call per device: the array's device address.
+static uint8_t *static_scratch_base(int dev) {
+    if (dev < 0 || dev >= 64) { set_err("quant_matvec_static: device ordinal out of range"); return nullptr; }
+    if (!g_static_base[dev]) {
+        void *p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+        if (e != cudaSuccess || !p) {
+            set_err(std::string("quant_matvec_static: cudaGetSymbolAddress failed: ") + cudaGetErrorString(e));
+            return nullptr;
+        }
+        g_static_base[dev] = static_cast<uint8_t *>(p);
+    }
+    return g_static_base[dev];
+}
+
+static bool matvec_static(const void *weights, size_t weights_size, uint32_t type, const float *input, float *output,
+                          size_t in, size_t out) {
+    uint32_t bb, row_bytes;
+    if (!matvec_args_ok(weights, weights_size, type, input, output, in, out, bb, row_bytes)) return false;
+    const size_t wbytes = out * (size_t)row_bytes;
+    const size_t off_w = round256(kStaticX + in * 4) + 256;
+    const size_t off_y = round256(off_w + wbytes) + 256;
+    const size_t need = off_y + round256(out * 4);
+    if (need > kStaticScratchBytes) {
+        set_err("quant_matvec_static: this call needs " + std::to_string(need) +
+                " bytes of device scratch; the static scratch holds " + std::to_string(kStaticScratchBytes) +
+                " (32 MiB): use quant_matvec for larger matrices");
+        return false;
+    }
+    int dev;
+    CK(cudaGetDevice(&dev));
+    uint8_t *base = static_scratch_base(dev);
+    if (!base) return false;
+    if (!set_smem_attrs(dev)) return false;
+    uint32_t *err = reinterpret_cast<uint32_t *>(base);
+    float *dx = reinterpret_cast<float *>(base + kStaticX);
+    uint8_t *dw = base + off_w;
+    float *dy = reinterpret_cast<float *>(base + off_y);
+    CK(cudaMemset(err, 0, 4));
+    CK(cudaMemcpy(dw, weights, wbytes, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(dx, input, in * 4, cudaMemcpyHostToDevice));
+    GemvLaunch L;
+    L.a.w = dw;
+    L.a.n_out = (uint32_t)out;
+    L.a.K = (uint32_t)in;
+    L.a.row_bytes = row_bytes;
+    L.a.x = dx;
+    L.a.y = dy;
+    L.a.err = err;
+    if (!plan_gemv((int)type, GM_STORE, num_sms(dev), L)) return false;
+    void *args[] = {&L.a};
+    CK(launch_ex(L.fn, L.grid, L.block, L.smem, nullptr, args, false));
+    CK(cudaMemcpy(output, dy, out * 4, cudaMemcpyDeviceToHost));
+    uint32_t e = 0;
+    CK(cudaMemcpy(&e, err, 4, cudaMemcpyDeviceToHost));
+    if (e) {
+        char b[80];
+        snprintf(b, sizeof b, "quant_matvec_static: device error word 0x%x", e);
+        set_err(b);
+        return false;
+    }
+    return true;
+}
+
+// --------------------------------------------------------------------------
 // model
 // --------------------------------------------------------------------------
 struct Mat {
@@ -886,6 +970,11 @@ int quant_matvec(const void *weights, size_t weights_size, uint32_t ggml_type, c
     if (dx) cudaFree(dx);
     if (dy) cudaFree(dy);
     return rc;
+}
+
+int quant_matvec_static(const void *weights, size_t weights_size, uint32_t ggml_type, const float *input,
+                        float *output, size_t input_size, size_t output_size) {
+    return matvec_static(weights, weights_size, ggml_type, input, output, input_size, output_size) ? 0 : -1;
 }
 
 int quant_matvec_dev(const void *d_weights, size_t weights_size, uint32_t ggml_type, const float *d_input,

@@ -54,6 +54,41 @@ int quant_matvec(const void *weights, size_t weights_size, uint32_t ggml_type,
                  size_t output_size);
 
 /*
+ * quant_matvec without any device allocation.  No counterpart in forword.c:
+ * the reference's quant_matvec (quant_matvec.h:7-15) runs on the CPU; the
+ * quant_matvec above keeps its signature but cudaMallocs and cudaFrees
+ * device copies of weights, input and output on every call.  This variant
+ * stages them in one fixed 32 MiB device array that is part of the library
+ * (one per device), so a call makes no cudaMalloc, cudaFree or other
+ * allocation.
+ *
+ * It is for callers that cannot allocate device memory at call time: a
+ * process whose own memory pool (a framework's caching allocator, a serving
+ * engine's KV-cache reservation) already holds the device's free memory, so
+ * cudaMalloc fails or fragments it; and latency-bound loops, where the
+ * implicit device-wide synchronisation of cudaFree would stall every other
+ * stream of the process.
+ *
+ * Same arguments, element types and -1 cases as quant_matvec, and also -1,
+ * with fwb_last_error() naming the bytes needed, when the call does not fit:
+ * 4*input_size + the weight rows + 4*output_size + about 1 KB of alignment
+ * must stay within 32 MiB (Q4_0 4096x4096 and 14336x4096 and Q8_0 4096x4096
+ * fit; Q8_0 14336x4096 does not).  Synchronous, on the legacy default stream
+ * of the current device.
+ *
+ * Set-up: the first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress) and sets kernel attributes; make that first call
+ * before any stream capture on that device.  Only the kernel's error word
+ * (the array's first 4 bytes) must be zero when the kernel starts; each call
+ * zeroes it before its launch.  All calls on a device share the array: calls
+ * that overlap in time on one device (from different host threads) race and
+ * corrupt each other's results, so serialise them.
+ */
+int quant_matvec_static(const void *weights, size_t weights_size, uint32_t ggml_type,
+                        const float *input, float *output, size_t input_size,
+                        size_t output_size);
+
+/*
  * Device-pointer form of quant_matvec for callers whose data already lives
  * in HBM.  d_weights must lie inside a cudaMalloc allocation and be 2-byte
  * aligned (the kernel reads up to 15 bytes either side of the rows, rounding
