@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """Batch-1 decode benchmark of forword.c's per-token forward on B200.
 
-Workload (N=1): the Llama-3-8B-shaped decoder with every linear weight in
+Workload (N=1, benchmark configuration 3): the Llama-3-8B-shaped decoder with every linear weight in
 GGUF Q4_0 (embedding and norms fp32), random-init N(0, 0.02) from a seed and
 written as a GGUF file.  A 512-token uniform-random prompt is fed through the
 per-token forward (the reference's own prompt loop, main.c:145-151), then
@@ -23,12 +23,16 @@ Arms
                     by oracle/Makefile into oracle/_ref, else the oracle's C
                     restatement), same model and positions, timed on the host.
 
-Multi-GPU (--gpus N under torchrun): every rank decodes its own replica of the
-8B model; there is no exchange between ranks, so the line reports
-"scaling": "weak" and value = all ranks' tokens / the slowest rank's time.
+Multi-GPU (--gpus N under torchrun): the Llama-70B-shaped Q4_0 model (benchmark
+configuration 5) decodes tensor-parallel over the N GPUs: every rank holds
+its slices of the weights, and the partial sums after o-proj and down-proj
+are added over NVLink inside the decode kernel.  One decode stream for the
+box ("scaling": "strong"); value = tokens/s of that stream, timed on the
+device on every rank, max over ranks.
 
-Every weight byte of a step is streamed from HBM (4.2 GB per token against a
-126 MB L2), so no explicit L2 flush is needed between steps.
+Every weight byte of a step is streamed from HBM (4.2 GB per token on one GPU
+for the 8B model, 39 GB / N per GPU for the 70B model, against a 126 MB L2),
+so no explicit L2 flush is needed between steps.
 """
 from __future__ import annotations
 
@@ -52,13 +56,48 @@ from fwb import configs, gguf_synth  # noqa: E402
 
 METRIC = "batch-1 decode tokens/s per box"
 UNIT = "tokens/s"
-PROMPT = 512
 MODEL_SEED = 1
 PROMPT_SEED = 2024
-CFG = configs.LLAMA8B_Q4_0
-WORKLOAD = ("llama-3-8B-shaped decoder, all linear weights Q4_0, fp32 embedding/norms, "
-            "random-init N(0,0.02); 512-token random prompt fed per token, then greedy "
-            "decode at batch 1")
+
+
+class Workload:
+    """The benchmark configuration one run measures.
+
+    N = 1: configuration 3 -- the Llama-3-8B shape, every linear weight Q4_0,
+    512-token prompt, greedy decode on one GPU.
+    N > 1: configuration 5 -- the Llama-70B shape, every linear weight Q4_0,
+    256-token prompt, greedy decode tensor-parallel over the N GPUs (one
+    decode stream for the whole box: strong scaling).
+    """
+
+    def __init__(self, world: int):
+        self.tp = world > 1
+        self.cfg = configs.LLAMA70B_Q4_0 if self.tp else configs.LLAMA8B_Q4_0
+        self.prompt = 256 if self.tp else 512
+        shape = "Llama-70B" if self.tp else "Llama-3-8B"
+        self.text = (f"{shape}-shaped decoder, all linear weights Q4_0, fp32 embedding/norms, "
+                     f"random-init N(0,0.02); {self.prompt}-token random prompt fed per token, then "
+                     f"greedy decode at batch 1" + (f", tensor parallel over {world} GPUs" if self.tp else ""))
+
+    def prompt_ids(self) -> np.ndarray:
+        return np.random.default_rng(PROMPT_SEED).integers(0, self.cfg.n_vocab, self.prompt).astype(np.uint32)
+
+    def kv_bytes_per_position(self, world: int = 1) -> int:
+        c = self.cfg
+        return 2 * c.n_layer * (c.n_head_kv // world) * c.head_dim * 4
+
+    def config(self, world: int, k_steps: int, w_steps: int, kv_ctx: int) -> dict:
+        return {
+            "workload": self.text,
+            "model": self.cfg.name,
+            "global_batch": 1,
+            "prompt_tokens": self.prompt,
+            "decode_positions": [self.prompt + w_steps, self.prompt + w_steps + k_steps],
+            "kv_ctx": kv_ctx,
+            "parallelism": f"tensor parallel x{world}" if world > 1 else "single GPU",
+            "l2": "inputs larger than L2: every step streams the model's quantised weights "
+                  f"({self.cfg.weight_bytes_per_token() / 1e9:.1f} GB per token)",
+        }
 
 
 def _args():
@@ -92,29 +131,8 @@ def _dist():
     return rank, world, local
 
 
-def _model_path(args) -> str:
-    return gguf_synth.cached_model(CFG, seed=MODEL_SEED, directory=args.model_dir)
-
-
-def _prompt() -> np.ndarray:
-    return np.random.default_rng(PROMPT_SEED).integers(0, CFG.n_vocab, PROMPT).astype(np.uint32)
-
-
-def _kv_bytes_per_position() -> int:
-    return 2 * CFG.n_layer * CFG.n_head_kv * CFG.head_dim * 4
-
-
-def _config(world: int, k_steps: int, w_steps: int, kv_ctx: int) -> dict:
-    return {
-        "workload": WORKLOAD,
-        "model": CFG.name,
-        "global_batch": 1,
-        "prompt_tokens": PROMPT,
-        "decode_positions": [PROMPT + w_steps, PROMPT + w_steps + k_steps],
-        "kv_ctx": kv_ctx,
-        "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-        "l2": "inputs larger than L2: every step streams the 4.2 GB of quantised weights",
-    }
+def _model_path(args, wl: Workload) -> str:
+    return gguf_synth.cached_model(wl.cfg, seed=MODEL_SEED, directory=args.model_dir)
 
 
 # ---------------------------------------------------------------------------
@@ -187,22 +205,23 @@ def _reference_model(path: str, kv_ctx: int):
     return pyoracle.OracleModel(path, max_ctx=kv_ctx), "port"
 
 
-def _time_reference(path: str, n_max: int, budget_s: float, warm: int = 1):
-    """Decode steps of the reference at positions PROMPT.. after a K/V pre-fill.
+def _time_reference(path: str, wl: Workload, n_max: int, budget_s: float, warm: int = 1):
+    """Decode steps of the reference at positions prompt.. after a K/V pre-fill.
 
     The prompt's K/V rows are written directly (N(0,1) values) instead of
-    running 512 prompt steps on the CPU (≈1 h for this model); each timed step
-    then does the same weight streaming and the same 512+ position attention as
+    running the prompt on the CPU (about an hour for the 8B model); each timed
+    step then does the same weight streaming and the same attention length as
     a real decode step.  Returns (tokens/s, steps timed, kind, seconds).
     """
+    c, P = wl.cfg, wl.prompt
     n_max = max(1, min(n_max, 512))
-    ref, kind = _reference_model(path, PROMPT + warm + n_max + 1)
+    ref, kind = _reference_model(path, P + warm + n_max + 1)
     rng = np.random.default_rng(7)
-    for layer in range(CFG.n_layer):
-        k = rng.standard_normal((PROMPT, CFG.n_head_kv, CFG.head_dim), dtype=np.float32)
-        v = rng.standard_normal((PROMPT, CFG.n_head_kv, CFG.head_dim), dtype=np.float32)
+    for layer in range(c.n_layer):
+        k = rng.standard_normal((P, c.n_head_kv, c.head_dim), dtype=np.float32)
+        v = rng.standard_normal((P, c.n_head_kv, c.head_dim), dtype=np.float32)
         ref.kv_load(layer, 0, k, v)
-    tok, pos = int(_prompt()[-1]), PROMPT
+    tok, pos = int(wl.prompt_ids()[-1]), P
     for _ in range(warm):
         tok = int(np.argmax(ref.forward(tok, pos)))
         pos += 1
@@ -222,16 +241,19 @@ def run_reference(args) -> None:
     rank, world, _ = _dist()
     if rank != 0:
         return
-    path = _model_path(args)
-    tps, n, kind, dt = _time_reference(path, args.steps, args.ref_budget_s, warm=1)
-    sample = (f"{n} greedy decode steps of the 8B Q4_0 model at positions {PROMPT + 1}..{PROMPT + n} "
-              f"after a 512-position K/V pre-fill (1 untimed warm-up step; {args.steps} requested, "
-              f"capped at {args.ref_budget_s:.0f} s)")
+    wl = Workload(args.gpus)
+    path = _model_path(args, wl)
+    tps, n, kind, dt = _time_reference(path, wl, args.steps, args.ref_budget_s, warm=1)
+    P = wl.prompt
+    sample = (f"{n} greedy decode steps of the {wl.cfg.name} model at positions {P + 1}..{P + n} after a "
+              f"{P}-position K/V pre-fill (1 untimed warm-up step; {args.steps} requested, capped at "
+              f"{args.ref_budget_s:.0f} s)")
     line = {
         "metric": METRIC, "value": tps, "unit": UNIT, "n_gpus": args.gpus, "steps": n,
-        "warmup": 1, "ms_per_step": dt / n * 1e3, "higher_is_better": True, "scaling": "weak",
+        "warmup": 1, "ms_per_step": dt / n * 1e3, "higher_is_better": True,
+        "scaling": "strong" if wl.tp else "weak",
         "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded random weights and prompt)",
-        "config": _config(1, n, 1, PROMPT + n + 2), "impl": "reference",
+        "config": wl.config(args.gpus, n, 1, P + n + 2), "impl": "reference",
         "cpu_baseline": {"value": tps, "unit": UNIT, "cores": 1, "kind": kind, "sample": sample,
                          "host_cores": os.cpu_count(),
                          "note": "the reference decode step is single-threaded by design"},
@@ -247,15 +269,18 @@ def run_b200(args) -> None:
     import torch
     import torch.distributed as dist
 
+    from fwb import tp
     from fwb.model import Model
 
     rank, world, local = _dist()
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    wl = Workload(world)
     torch.cuda.set_device(local)
     if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900),
-                                device_id=torch.device(f"cuda:{local}"))
+        # host coordination only (IPC handles, barriers, the max over ranks):
+        # the decode path's exchange runs over NVLink inside the kernel
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=1800))
 
     def barrier():
         if world > 1:
@@ -264,33 +289,33 @@ def run_b200(args) -> None:
     def max_over_ranks(x: float) -> float:
         if world == 1:
             return x
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        t = torch.tensor([x], dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
     if rank == 0:
-        path = _model_path(args)
+        path = _model_path(args, wl)
     barrier()
     if rank != 0:
-        path = _model_path(args)
+        path = _model_path(args, wl)
 
     K, W = args.steps, args.warmup
     if K < 1 or W < 0:
         raise SystemExit("--steps must be >= 1 and --warmup >= 0")
-    need = PROMPT + 2 * (W + K) + 1
+    P = wl.prompt
+    need = P + 2 * (W + K) + 1
     kv_ctx = max(1024, 1 << (need - 1).bit_length())
-    if kv_ctx > CFG.n_ctx:
-        raise SystemExit(f"--steps/--warmup need {need} positions > n_ctx {CFG.n_ctx}")
+    if kv_ctx > wl.cfg.n_ctx:
+        raise SystemExit(f"--steps/--warmup need {need} positions > n_ctx {wl.cfg.n_ctx}")
 
-    m = Model(path, max_ctx=kv_ctx, device=local)
+    m = tp.open_model(path, kv_ctx, rank, world, local) if world > 1 else Model(path, max_ctx=kv_ctx, device=local)
     stream = torch.cuda.ExternalStream(m.stream, device=torch.device(f"cuda:{local}"))
 
     # prompt: one forward per token (teacher forced), as the reference's main loop
-    prompt = _prompt()
     tok = 0
-    for i, t in enumerate(prompt):
+    for i, t in enumerate(wl.prompt_ids()):
         tok = m.forward_argmax(int(t), i)
-    pos = PROMPT
+    pos = P
 
     # warm-up
     if W:
@@ -320,7 +345,8 @@ def run_b200(args) -> None:
     ms = max_over_ranks(e0.elapsed_time(e1))
     tok, pos = int(toks[-1]), pos + K
 
-    # ---- end to end through fwb_forward with host buffers ----
+    # ---- end to end through fwb_forward with host buffers (every rank gets
+    # ---- the full logits and picks the same token)
     logits = torch.empty(m.n_vocab, dtype=torch.float32, pin_memory=True).numpy()
     for _ in range(min(W, 3)):  # first use of the pinned logits path
         m.forward(tok, pos, out=logits)
@@ -339,49 +365,53 @@ def run_b200(args) -> None:
     ms_e2e = max_over_ranks(f0.elapsed_time(f1))
 
     kernels = m.kernels_per_step
-    weight_bytes = m.weight_bytes
+    weight_bytes = m.weight_bytes  # this rank's slices
     m.close()
     clk = clocks.finish() if clocks else None
 
     if rank == 0:
         peak, peak_kind = _peaks()
-        # algorithmic bytes of one decode-kernel launch at position p: every
-        # weight byte once, the K/V rows 0..p once, the new K/V row, the logits
-        kvp = _kv_bytes_per_position()
+        # algorithmic bytes of one decode-kernel launch on one GPU at position
+        # p: every weight byte of its slices once, its K/V rows 0..p once, the
+        # new K/V row, its logits
+        kvp = wl.kv_bytes_per_position(world)
         mean_pos = pos_timed + (K - 1) / 2.0
-        step_bytes = weight_bytes + kvp * (mean_pos + 1) + kvp + 4 * CFG.n_vocab
+        step_bytes = weight_bytes + kvp * (mean_pos + 1) + kvp + 4 * wl.cfg.n_vocab // world
         launch_s = ms / 1e3 / K
         achieved = step_bytes / launch_s / 1e9
         line = {
-            "metric": METRIC, "value": world * K / (ms / 1e3), "unit": UNIT, "n_gpus": world,
+            "metric": METRIC, "value": K / (ms / 1e3), "unit": UNIT, "n_gpus": world,
             "steps": K, "warmup": W, "ms_per_step": ms / K, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None,
+            "scaling": "strong" if wl.tp else "weak", "vs_baseline": None,
             "dtype": "q4_0 weights x 16-bit block fixed-point activations (dp4a), fp32 accumulate",
             "data": "synthetic (seeded random weights and prompt)",
-            "config": _config(world, K, W, kv_ctx),
+            "config": wl.config(world, K, W, kv_ctx),
             "roofline": {
                 "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "peak_source": f"hbm_gbs ({peak_kind})",
-                "traffic": _ncu_traffic(),
-                "kernel": "decode_kernel (persistent, one launch per token)",
+                "traffic": None if wl.tp else _ncu_traffic(),
+                "kernel": "decode_kernel (persistent, one launch per token" +
+                          (", per GPU)" if wl.tp else ")"),
                 "bytes_per_launch": step_bytes,
                 "frac_weights_only": weight_bytes / launch_s / 1e9 / peak,
                 "launch_time": "events over the K timed launches / K (includes the 8-byte "
                                "step-counter memset node of each graph)",
             },
-            "e2e": {"value": world * K / (ms_e2e / 1e3), "unit": UNIT,
-                    "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4 * CFG.n_vocab + 8,
+            "e2e": {"value": K / (ms_e2e / 1e3), "unit": UNIT,
+                    "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4 * wl.cfg.n_vocab + 8,
                     "api": "fwb_forward (transformer_forward) with pinned host logits, host argmax"},
             "clocks": clk,
             "gpu_launches": kernels * K,
         }
+        if wl.tp:
+            line["roofline"]["note"] = ("per GPU: its weight slices; the box-wide tokens/s is the value "
+                                        "(one decode stream across all GPUs)")
         if world == 1 and not args.no_cpu_baseline:
-            tps, n, kind, dt = _time_reference(path, 1 << 30, args.cpu_budget_s, warm=1)
+            tps, n, kind, dt = _time_reference(path, wl, 1 << 30, args.cpu_budget_s, warm=1)
             line["cpu_baseline"] = {
                 "value": tps, "unit": UNIT, "cores": 1, "kind": kind, "host_cores": os.cpu_count(),
                 "sample": f"{n} greedy decode steps of the same model at positions "
-                          f"{PROMPT + 1}..{PROMPT + n} after a 512-position K/V pre-fill "
-                          f"({dt:.1f} s)"}
+                          f"{P + 1}..{P + n} after a {P}-position K/V pre-fill ({dt:.1f} s)"}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

@@ -32,7 +32,7 @@ struct AttnArgs {
 };
 
 constexpr int kAttnWarps = 4;          // warps per CTA of the standalone kernel
-constexpr uint32_t kMinSplitPos = 256;  // positions per split at least
+constexpr uint32_t kMinSplitPos = 64;   // positions per split at least
 constexpr uint32_t kMaxSplits = 64;
 
 // Splits in use at n_pos positions (short contexts merge few partials).
@@ -46,7 +46,8 @@ struct AttnSmem {
     float pbuf[NW][32];
     float wm[NW][GQ], wl[NW][GQ];
     float wo[NW][GQ][HD];
-    float sw[kMaxSplits][GQ];
+    float wf[NW][GQ], wM[GQ];  // per-warp rescale factors exp(m_w - M) and the CTA maximum
+    float sw[kMaxSplits][GQ], sl[kMaxSplits][GQ];
     float sL[GQ];
     uint32_t last_flag;
 };
@@ -169,16 +170,22 @@ __device__ void attn_item(const AttnArgs &a, uint32_t h, uint32_t sp, uint32_t n
             for (int d = 0; d < 4; ++d) sh.wo[warp][g][4 * lane + d] = o[g][d];
     }
     __syncthreads();
+    // rescale factor of every (warp, head), once: exp(m_w - M)
+    if (tid < (uint32_t)(NW * GQ)) {
+        const uint32_t w = tid / GQ, g = tid % GQ;
+        float M = sh.wm[0][g];
+        for (int v = 1; v < NW; ++v) M = fmaxf(M, sh.wm[v][g]);
+        sh.wf[w][g] = sh.wm[w][g] == -INFINITY ? 0.f : expf(sh.wm[w][g] - M);
+        if (w == 0) sh.wM[g] = M;
+    }
+    __syncthreads();
     if (n_use == 1) {  // the only split: normalise and write the output directly
         for (uint32_t i = tid; i < (uint32_t)(GQ * HD); i += blockDim.x) {
             const uint32_t g = i / HD, d = i % HD;
-            float M = sh.wm[0][g];
-            for (int w = 1; w < NW; ++w) M = fmaxf(M, sh.wm[w][g]);
             float L = 0.f, O = 0.f;
             for (int w = 0; w < NW; ++w) {
-                const float f = sh.wm[w][g] == -INFINITY ? 0.f : expf(sh.wm[w][g] - M);
-                L = fmaf(sh.wl[w][g], f, L);
-                O = fmaf(sh.wo[w][g][d], f, O);
+                L = fmaf(sh.wl[w][g], sh.wf[w][g], L);
+                O = fmaf(sh.wo[w][g][d], sh.wf[w][g], O);
             }
             a.out[(size_t)(h * GQ + g) * HD + d] = __fdiv_rn(O, L);
         }
@@ -188,16 +195,13 @@ __device__ void attn_item(const AttnArgs &a, uint32_t h, uint32_t sp, uint32_t n
     float *pp = a.part + ((size_t)h * a.n_split + sp) * GQ * (HD + 2);
     for (uint32_t i = tid; i < (uint32_t)(GQ * HD); i += blockDim.x) {
         const uint32_t g = i / HD, d = i % HD;
-        float M = sh.wm[0][g];
-        for (int w = 1; w < NW; ++w) M = fmaxf(M, sh.wm[w][g]);
         float L = 0.f, O = 0.f;
         for (int w = 0; w < NW; ++w) {
-            const float f = sh.wm[w][g] == -INFINITY ? 0.f : expf(sh.wm[w][g] - M);
-            L = fmaf(sh.wl[w][g], f, L);
-            O = fmaf(sh.wo[w][g][d], f, O);
+            L = fmaf(sh.wl[w][g], sh.wf[w][g], L);
+            O = fmaf(sh.wo[w][g][d], sh.wf[w][g], O);
         }
         pp[g * (HD + 2) + 2 + d] = O;
-        if (d == 0) { pp[g * (HD + 2)] = M; pp[g * (HD + 2) + 1] = L; }
+        if (d == 0) { pp[g * (HD + 2)] = sh.wM[g]; pp[g * (HD + 2) + 1] = L; }
     }
     __threadfence();
     __syncthreads();
@@ -209,7 +213,12 @@ __device__ void attn_item(const AttnArgs &a, uint32_t h, uint32_t sp, uint32_t n
         // exp(m_s - M) (one load per (split, head)), then every output element
         // sums its split values with independent L2 loads
         const float *P = a.part + (size_t)h * a.n_split * GQ * (HD + 2);
-        for (uint32_t i = tid; i < n_use * GQ; i += blockDim.x) sh.sw[i / GQ][i % GQ] = __ldcg(P + (size_t)i * (HD + 2));
+        // every (m, l) pair with one load each, all in flight; then shared
+        // memory only
+        for (uint32_t i = tid; i < n_use * GQ; i += blockDim.x) {
+            sh.sw[i / GQ][i % GQ] = __ldcg(P + (size_t)i * (HD + 2));
+            sh.sl[i / GQ][i % GQ] = __ldcg(P + (size_t)i * (HD + 2) + 1);
+        }
         __syncthreads();
         if (tid < (uint32_t)GQ) {
             float M = -INFINITY;
@@ -217,17 +226,26 @@ __device__ void attn_item(const AttnArgs &a, uint32_t h, uint32_t sp, uint32_t n
             float L = 0.f;
             for (uint32_t s = 0; s < n_use; ++s) {
                 const float f = sh.sw[s][tid] == -INFINITY ? 0.f : expf(sh.sw[s][tid] - M);
-                L = fmaf(__ldcg(P + ((size_t)s * GQ + tid) * (HD + 2) + 1), f, L);
+                L = fmaf(sh.sl[s][tid], f, L);
                 sh.sw[s][tid] = f;
             }
             sh.sL[tid] = L;
         }
         __syncthreads();
+        // outputs: the split values of an element are loaded 16 at a time
+        // before they are summed (in split order)
         for (uint32_t i = tid; i < (uint32_t)(GQ * HD); i += blockDim.x) {
             const uint32_t g = i / HD, d = i % HD;
             float O = 0.f;
-#pragma unroll 8
-            for (uint32_t s = 0; s < n_use; ++s) O = fmaf(__ldcg(P + ((size_t)s * GQ + g) * (HD + 2) + 2 + d), sh.sw[s][g], O);
+            for (uint32_t s0 = 0; s0 < n_use; s0 += 16) {
+                float v[16];
+#pragma unroll
+                for (uint32_t k = 0; k < 16; ++k)
+                    v[k] = s0 + k < n_use ? __ldcg(P + ((size_t)(s0 + k) * GQ + g) * (HD + 2) + 2 + d) : 0.f;
+#pragma unroll
+                for (uint32_t k = 0; k < 16; ++k)
+                    if (s0 + k < n_use) O = fmaf(v[k], sh.sw[s0 + k][g], O);
+            }
             a.out[(size_t)(h * GQ + g) * HD + d] = __fdiv_rn(O, sh.sL[g]);
         }
         if (tid == 0) a.ticket[h] = 0;

@@ -96,6 +96,15 @@ __device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
+// 16-byte asynchronous copy global -> shared (no register staging); both
+// addresses 16-byte aligned.  Completed by cp_async_wait_all() in the issuing
+// thread, visible to the CTA after a following barrier.
+__device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // gpu-scope release add / acquire load (grid barrier)
 __device__ __forceinline__ void red_release_add(uint32_t *p, uint32_t v) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");

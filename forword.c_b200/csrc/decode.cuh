@@ -28,14 +28,35 @@ struct EmbedArgs {
     float *x;
 };
 
-enum PhaseKind : uint32_t { PH_EMBED = 0, PH_GEMV = 1, PH_ATTN = 2 };
+// Tensor parallelism: sum of the ranks' partial outputs (all-reduce), read
+// straight from every rank's exchange buffer over NVLink (peer pointers; no
+// multicast), added to the residual x.  Every rank sums in rank order, so all
+// ranks hold bit-identical x afterwards.
+constexpr uint32_t kMaxRanks = 8;
+struct ArArgs {
+    float *x;                      // [n] residual stream of this rank (x += sum of parts)
+    const float *part[kMaxRanks];  // every rank's partial output of this phase
+    uint32_t n, world;
+};
+// Tensor parallelism: the greedy token from the ranks' (value, index)
+// candidates (lowest index among equal maxima, as sampler_argmax).
+struct TpArgmaxArgs {
+    const float *cand[kMaxRanks];  // every rank's candidate pair
+    uint32_t world;
+    uint32_t *out_token, *step_rw, *hist;
+};
 
-struct Phase {
+enum PhaseKind : uint32_t { PH_EMBED = 0, PH_GEMV = 1, PH_ATTN = 2, PH_ALLREDUCE = 3, PH_TPARGMAX = 4 };
+
+struct __align__(16) Phase {
     uint32_t kind, qt, mode, a4;  // PH_GEMV: quant type, mode, 4-byte-aligned units
     uint32_t hd, gq;              // PH_ATTN: head_dim, GQA group
+    uint32_t gsync;               // the barrier before this phase spans every rank
     GemvArgs g;
     AttnArgs at;
     EmbedArgs e;
+    ArArgs ar;
+    TpArgmaxArgs am;
 };
 
 // This CTA's weight stream of one GEMV phase (host-computed).
@@ -60,7 +81,15 @@ struct DecodeArgs {
     uint32_t *sync;        // [0] barrier arrivals (zeroed before each launch), [1] abort
     uint32_t *err;
     uint32_t *n_st_cta;    // [gridDim.x] stages of each CTA
+    // tensor parallelism (world > 1): cross-rank barrier counters (every rank's,
+    // mapped; each CTA of each rank adds 1 to all of them per barrier), and the
+    // number of such barriers completed before this step ([0], advanced by
+    // n_gsync at the end of the step by CTA 0)
+    unsigned long long *gcount[kMaxRanks];
+    unsigned long long *gbase;
+    uint32_t world, n_gsync;
     unsigned long long *trace;  // optional: CTA 0's globaltimer at phase start [2p] and barrier arrival [2p+1]
+    unsigned long long *trace_cta;  // optional: every CTA's barrier arrival [p * gridDim.x + cta]
 };
 
 __device__ __forceinline__ unsigned long long global_ns() {
@@ -121,15 +150,40 @@ struct PhaseResult {
     bool ok;
 };
 
+// L2 prefetch of the K and V rows that this CTA's work items of the attention
+// phase `at` will read (the same item split as attn_phase_t).
+__device__ void prefetch_attn_kv(const AttnArgs &at, uint32_t hd, uint32_t pos) {
+    const uint32_t n_pos = pos + 1, n_use = attn_splits_in_use(at, n_pos);
+    const uint32_t chunk = (n_pos + n_use - 1) / n_use;
+    for (uint32_t it = blockIdx.x; it < at.n_kv * n_use; it += gridDim.x) {
+        const uint32_t h = it / n_use, sp = it % n_use;
+        const uint32_t c0 = min(n_pos, sp * chunk), c1 = min(n_pos, c0 + chunk);
+        if (c1 <= c0) continue;
+        const size_t off = ((size_t)h * at.kv_ctx + c0) * hd;
+        const uint32_t bytes = (c1 - c0) * hd * 4u;
+        bulk_prefetch_l2(at.kc + off, bytes);
+        bulk_prefetch_l2(at.vc + off, bytes);
+    }
+}
+
 // Grid-wide barrier number `epoch` (1, 2, ...).  Bounded: on timeout, or
-// when another CTA already gave up, it sets the abort flag and returns false.
-__device__ bool grid_sync(uint32_t *sync, uint32_t epoch, uint32_t *err) {
+// when another CTA already gave up (the abort flag sync[1]), it sets the
+// abort flag and returns false.  While waiting, the CTAs start the next
+// phase `nx`'s first reads that miss L2: a GEMV's RMSNorm weight (128 bytes
+// per CTA) or the attention phase's K/V rows.
+__device__ bool grid_sync(uint32_t *sync, uint32_t epoch, uint32_t *err, const Phase *nx) {
     __shared__ uint32_t ok_flag;
     __syncthreads();
     if (threadIdx.x == 0) {
+        const bool kv = nx && nx->kind == PH_ATTN;
+        const uint32_t pos = kv ? __ldcg(&nx->at.step[1]) : 0u;
         // release: this CTA's writes of the phase become visible with the add;
         // acquire: the other CTAs' writes are visible once the count is seen
         red_release_add(&sync[0], 1u);
+        if (nx && nx->kind == PH_GEMV && nx->g.norm && blockIdx.x * 128u < nx->g.K * 4u)
+            bulk_prefetch_l2(reinterpret_cast<const uint8_t *>(nx->g.norm_w) + blockIdx.x * 128u,
+                             min(128u, nx->g.K * 4u - blockIdx.x * 128u));
+        if (kv && pos < nx->at.kv_ctx) prefetch_attn_kv(nx->at, nx->hd, pos);
         const uint32_t target = epoch * gridDim.x;
         uint32_t ok = 0;
         for (uint32_t i = 0; i < (1u << 25); ++i) {
@@ -147,6 +201,79 @@ __device__ bool grid_sync(uint32_t *sync, uint32_t epoch, uint32_t *err) {
     }
     __syncthreads();
     return ok_flag != 0;
+}
+
+__device__ __forceinline__ void red_release_sys_add64(unsigned long long *p, unsigned long long v) {
+    asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys64(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Barrier across every CTA of every rank (tensor parallelism): each CTA adds
+// one to every rank's counter (release, system scope: its writes of the phase
+// become visible to the peers) and waits (acquire) until its own counter shows
+// all world * gridDim.x arrivals of barrier `target / (world * gridDim.x)`.
+// Bounded like grid_sync; a timeout sets the local abort flag and the error.
+__device__ bool global_sync(const DecodeArgs &d, unsigned long long target) {
+    __shared__ uint32_t ok_flag;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (uint32_t q = 0; q < d.world; ++q) red_release_sys_add64(d.gcount[q], 1ull);
+        const unsigned long long *mine = d.gcount[0];
+        uint32_t ok = 0;
+        for (uint32_t i = 0; i < (1u << 25); ++i) {
+            if (ld_acquire_sys64(mine) >= target) { ok = 1; break; }
+            if ((i & 255) == 255) {
+                if (ld_acquire(&d.sync[1])) break;
+                __nanosleep(64);
+            }
+        }
+        if (!ok) {
+            atomicOr(d.err, ERR_GRID_SYNC);
+            atomicExch(&d.sync[1], 1u);
+        }
+        ok_flag = ok;
+    }
+    __syncthreads();
+    return ok_flag != 0;
+}
+
+// x[i] += sum over ranks of part_q[i] for this CTA's rows (peer loads bypass L1).
+__device__ void allreduce_phase(const ArArgs &a) {
+    const uint32_t b = (uint32_t)((uint64_t)blockIdx.x * a.n / gridDim.x);
+    const uint32_t e = (uint32_t)((uint64_t)(blockIdx.x + 1) * a.n / gridDim.x);
+    for (uint32_t i = b + threadIdx.x; i < e; i += blockDim.x) {
+        float v[kMaxRanks];
+#pragma unroll
+        for (uint32_t q = 0; q < kMaxRanks; ++q) v[q] = q < a.world ? __ldcg(a.part[q] + i) : 0.f;
+        float t = v[0];
+#pragma unroll
+        for (uint32_t q = 1; q < kMaxRanks; ++q)
+            if (q < a.world) t = __fadd_rn(t, v[q]);
+        a.x[i] = __fadd_rn(__ldcg(&a.x[i]), t);
+    }
+}
+
+__device__ void tp_argmax_phase(const TpArgmaxArgs &a) {
+    if (blockIdx.x != 0 || threadIdx.x != 0) return;
+    float bv = -INFINITY;
+    uint32_t bi = 0xffffffffu;
+    for (uint32_t q = 0; q < a.world; ++q) {
+        const float cv = __ldcg(a.cand[q]);
+        const uint32_t ci = __ldcg(reinterpret_cast<const uint32_t *>(a.cand[q]) + 1);
+        if (ci != 0xffffffffu && (bi == 0xffffffffu || cv > bv || (cv == bv && ci < bi))) { bv = cv; bi = ci; }
+    }
+    const uint32_t nxt = bi == 0xffffffffu ? 0u : bi;  // every logit NaN: index 0, as the reference
+    *a.out_token = nxt;
+    if (a.hist) {
+        const uint32_t p = __ldcg(&a.step_rw[1]);
+        a.hist[p] = nxt;
+        a.step_rw[0] = nxt;
+        a.step_rw[1] = p + 1;
+    }
 }
 
 template <int HD, int GQ>
@@ -201,7 +328,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
     extern __shared__ __align__(128) uint8_t smem[];
     const uint32_t tid = threadIdx.x;
     const uint32_t ring_off = kHeaderBytes + d.scratch_bytes;
-    GemvSmem sm = gemv_smem(smem, 32);
+    GemvSmem sm = gemv_smem(smem, 32, 0);
     sm.ring = smem + ring_off;
     StageSrc *tab = reinterpret_cast<StageSrc *>(smem + ring_off + d.NS * d.stage_bytes + 128);
     const uint32_t total = d.n_st_cta[blockIdx.x];
@@ -228,6 +355,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
     }
 
     RingState rs{0, 0, 0};
+    // cross-rank barriers completed before this step, and during it
+    const unsigned long long gbase = d.world > 1 ? __ldcg(d.gbase) : 0ull;
+    uint32_t gk = 0;
     bool ok = true;
     // phase descriptors are staged in shared memory one phase ahead
     __shared__ __align__(16) Phase ph_buf[2];
@@ -235,17 +365,23 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
     for (uint32_t i = tid; i < kPhWords; i += blockDim.x)
         reinterpret_cast<uint32_t *>(&ph_buf[0])[i] = reinterpret_cast<const uint32_t *>(d.ph)[i];
     __syncthreads();
+    constexpr uint32_t kPhChunks = sizeof(Phase) / 16;
+    static_assert(sizeof(Phase) % 16 == 0 && kPhChunks <= kDecodeThreads, "phase descriptor copy");
     for (uint32_t p = 0; p < d.n_ph; ++p) {
         const Phase &P = ph_buf[p & 1];
-        if (p + 1 < d.n_ph)
-            for (uint32_t i = tid; i < kPhWords; i += blockDim.x)
-                reinterpret_cast<uint32_t *>(&ph_buf[(p + 1) & 1])[i] =
-                    reinterpret_cast<const uint32_t *>(d.ph + p + 1)[i];
+        // the next descriptor streams into the other buffer while this phase runs
+        const bool next = p + 1 < d.n_ph;
+        if (next && tid < kPhChunks) {
+            cp_async16(reinterpret_cast<uint8_t *>(&ph_buf[(p + 1) & 1]) + 16 * tid,
+                       reinterpret_cast<const uint8_t *>(d.ph + p + 1) + 16 * tid);
+            cp_async_commit();
+        }
         if (d.trace && blockIdx.x == 0 && tid == 0) d.trace[2 * p] = global_ns();
-        if (ok && !__ldcg(&d.sync[1])) {
+        if (ok) {
             if (P.kind == PH_GEMV) {
                 sm.planes = reinterpret_cast<uint32_t *>(smem + kHeaderBytes);
                 sm.nbp = ((P.g.K / 32) + 1) & ~1u;
+                sm.red = reinterpret_cast<float *>(smem + kHeaderBytes + plane_bytes(P.g.K));
                 PhaseResult r{rs, false};
                 switch (P.qt) {
                 case QT_Q4_0: r = gemv_phase_q<QT_Q4_0>(P, sm, rs, tab, d.n_ph, total, d.NS, d.stage_bytes); break;
@@ -257,6 +393,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
                 ok = ok && r.ok;
             } else if (P.kind == PH_ATTN) {
                 attn_phase(P, smem + kHeaderBytes);
+            } else if (P.kind == PH_ALLREDUCE) {
+                allreduce_phase(P.ar);
+            } else if (P.kind == PH_TPARGMAX) {
+                tp_argmax_phase(P.am);
             } else {  // PH_EMBED: x = row step[0] of the table (linear_get_row, linear.c:60-151)
                 const EmbedArgs &e = P.e;
                 const uint32_t tok = __ldcg(&e.step[0]);
@@ -271,13 +411,34 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
             // accounted for, without computing
             ok = false;
         }
-        if (d.trace && blockIdx.x == 0) {
+        if (d.trace) {
             __syncthreads();
-            if (tid == 0) d.trace[2 * p + 1] = global_ns();
+            if (tid == 0) {
+                const unsigned long long t = global_ns();
+                if (blockIdx.x == 0) d.trace[2 * p + 1] = t;
+                d.trace_cta[(size_t)p * gridDim.x + blockIdx.x] = t;
+            }
         }
-        if (p + 1 < d.n_ph && !grid_sync(d.sync, p + 1, d.err)) ok = false;
+        if (next && tid < kPhChunks) cp_async_wait_all();
+        // (the barriers' leading __syncthreads makes the copied descriptor visible)
+        if (next) {
+            const Phase &N = ph_buf[(p + 1) & 1];
+            // a phase after a cross-rank barrier is preceded by that barrier only:
+            // it includes every local CTA, so the local count is advanced too
+            // (grid_sync counts epochs by phase index)
+            __syncthreads();
+            if (N.gsync) {
+                ++gk;
+                if (!global_sync(d, (gbase + gk) * (unsigned long long)d.world * gridDim.x)) ok = false;
+                if (tid == 0) red_release_add(&d.sync[0], 1u);
+            } else if (!grid_sync(d.sync, p + 1, d.err, &N)) {
+                ok = false;
+            }
+        }
     }
     if (d.trace && blockIdx.x == 0 && tid == 0) d.trace[2 * d.n_ph] = global_ns();
+    // every CTA read gbase before the first barrier of the step
+    if (d.world > 1 && blockIdx.x == 0 && tid == 0) *d.gbase = gbase + d.n_gsync;
     if (!ok && tid == 0) ring_drain(sm, min(total, rs.j + d.NS), d.NS, d.err);
 }
 

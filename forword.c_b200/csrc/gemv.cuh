@@ -32,10 +32,13 @@
 // per value; about 3e-6 relative on a block dot of typical inputs) and a few
 // final float operations per block.
 //
-// Reduction.  Rows are processed in batches of 8 rounds; the 8 partial sums
-// per thread are reduced across the unit lanes with a butterfly
-// reduce-scatter (7 + log2(G/8) shuffles per 8 rows), then across warps in
-// shared memory, and the epilogue runs on the finished rows.
+// Reduction.  Rows are processed in batches of 8 per thread; the 8 partial
+// sums are reduced across the unit lanes of a warp with a butterfly
+// reduce-scatter (7 + log2(G/8) shuffles per 8 rows) and parked in shared
+// memory per warp, with no CTA-wide barrier inside the row loop.  After the
+// last round one barrier, then the sums across the warps of a slot and the
+// fused epilogue over all of the CTA's rows, whose operands (residual, RoPE
+// factors) were fetched before the loop.
 #pragma once
 #include "common.cuh"
 
@@ -64,7 +67,7 @@ enum InMode : int { IN_PLAIN = 0, IN_RMSNORM = 1 };
 constexpr int kRB = 8;              // rows per reduction batch (per slot): 4 rounds x 2 rows
 constexpr int kMaxStages = 8;
 constexpr uint32_t kMaxConsumers = 512;  // threads per GEMV CTA (all consumers)
-constexpr uint32_t kHeaderBytes = 4096;
+constexpr uint32_t kHeaderBytes = 1024;  // barriers, stage counters, small scratch
 constexpr uint32_t kStageSlack = 128;  // alignment + half-unit over-read room
 constexpr int kXMax = 32767;        // fixed-point range of the inputs (16 bits per value)
 
@@ -81,6 +84,7 @@ struct GemvArgs {
     uint32_t R;          // local rows per stage (multiple of S; even for pair modes)
     uint32_t NS;         // ring stages
     uint32_t stage_bytes;
+    uint32_t red_bytes;  // shared partial row sums: (Upad/32 or 1) floats per local row
     const float *x;      // input [K]
     const float *norm_w; // RMSNorm weight [K]
     float eps;
@@ -94,6 +98,9 @@ struct GemvArgs {
     uint32_t *am_idx, *ticket, *out_token;
     const uint32_t *step;  // [0] token, [1] pos
     uint32_t *step_rw, *hist;  // GM_LOGITS: advance step[0..1], record hist[pos]
+    uint32_t idx_base;     // GM_LOGITS: vocabulary index of row 0 (a tensor-parallel rank's slice)
+    float *tp_cand;        // GM_LOGITS under tensor parallelism: (value, index) of this rank's
+                           // maximum goes here instead of advancing the step
     uint32_t *err;
     // optional profile: thread 0 of each CTA adds ns spent in
     // [0] prologue (norm + planes), [1] waiting for stages, [2] the row loop, [3] tail
@@ -191,7 +198,9 @@ __device__ __forceinline__ void load_unit_words(const uint8_t *p, uint32_t (&w)[
     }
 }
 
-// Partial dot of one unit: block A always, block B when `two`.
+// Partial dot of one unit: block A, plus block B when `two` (computed either
+// way and selected, so the row loop has no divergent branch; the bytes read
+// past the end of a row with an odd block count stay inside the stage slack).
 template <int QT, bool A4>
 __device__ __forceinline__ float unit_dot(const uint8_t *p, const XBlock &xa, const XBlock &xb, bool two) {
     if constexpr (QT == QT_Q4_0) {
@@ -199,37 +208,31 @@ __device__ __forceinline__ float unit_dot(const uint8_t *p, const XBlock &xa, co
         load_unit_words<9, A4>(p, w);
         uint32_t qa[4] = {__funnelshift_r(w[0], w[1], 16), __funnelshift_r(w[1], w[2], 16),
                           __funnelshift_r(w[2], w[3], 16), __funnelshift_r(w[3], w[4], 16)};
-        float r = dot_q4_0(qa, w[0], xa);
-        if (two) {
-            uint32_t qb[4] = {w[5], w[6], w[7], w[8]};
-            r += dot_q4_0(qb, w[4] >> 16, xb);
-        }
-        return r;
+        const float r = dot_q4_0(qa, w[0], xa);
+        const uint32_t qb[4] = {w[5], w[6], w[7], w[8]};
+        const float r2 = dot_q4_0(qb, w[4] >> 16, xb);
+        return two ? r + r2 : r;
     } else if constexpr (QT == QT_Q5_0) {
         uint32_t w[11];
         load_unit_words<11, A4>(p, w);
         uint32_t qa[4] = {__funnelshift_r(w[1], w[2], 16), __funnelshift_r(w[2], w[3], 16),
                           __funnelshift_r(w[3], w[4], 16), __funnelshift_r(w[4], w[5], 16)};
-        float r = dot_q5_0(__funnelshift_r(w[0], w[1], 16), qa, w[0], xa);
-        if (two) {
-            uint32_t qb[4] = {w[7], w[8], w[9], w[10]};
-            r += dot_q5_0(w[6], qb, w[5] >> 16, xb);
-        }
-        return r;
+        const float r = dot_q5_0(__funnelshift_r(w[0], w[1], 16), qa, w[0], xa);
+        const uint32_t qb[4] = {w[7], w[8], w[9], w[10]};
+        const float r2 = dot_q5_0(w[6], qb, w[5] >> 16, xb);
+        return two ? r + r2 : r;
     } else {
         uint32_t w[17];
         load_unit_words<17, A4>(p, w);
         uint32_t qa[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) qa[k] = __funnelshift_r(w[k], w[k + 1], 16);
-        float r = dot_q8_0(qa, w[0], xa);
-        if (two) {
-            uint32_t qb[8];
+        const float r = dot_q8_0(qa, w[0], xa);
+        uint32_t qb[8];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) qb[k] = w[9 + k];
-            r += dot_q8_0(qb, w[8] >> 16, xb);
-        }
-        return r;
+        for (int k = 0; k < 8; ++k) qb[k] = w[9 + k];
+        const float r2 = dot_q8_0(qb, w[8] >> 16, xb);
+        return two ? r + r2 : r;
     }
 }
 
@@ -275,19 +278,19 @@ __device__ __forceinline__ void cta_rows(uint32_t n_out, uint32_t g, uint32_t &b
 }
 
 // ---------------------------------------------------------------------------
-// one GEMV, split into a producer (one thread) and consumers (NC threads).
-// Stage k of the CTA lives in ring slot kring % NS, phase parity
-// (kring / NS) & 1, where kring counts stages from the start of the ring, so
-// several GEMVs can run back to back through one ring.
+// Shared memory of one GEMV.  Stage k of the CTA lives in ring slot
+// kring % NS, phase parity (kring / NS) & 1, where kring counts stages from
+// the start of the ring, so several GEMVs can run back to back through one
+// ring.
 // ---------------------------------------------------------------------------
-
 struct GemvSmem {
     uint64_t *full;   // [kMaxStages] stage landed (transaction count)
-    uint32_t *done;   // [kMaxStages] consumer warps finished with the slot
-    float *red, *out_tile, *misc;
-    uint32_t *misc_u;
-    uint32_t *planes;  // quantised input: word (p*8+k)*nbp + b (p 0 = high, 1 = low), s at 16*nbp + b, nx at 17*nbp + b
-    uint32_t nbp;      // blocks of the input, rounded up to even
+    uint32_t *done;   // [kMaxStages] warps finished with the slot, then the refill cursor
+    float *misc;      // [64]
+    uint32_t *misc_u; // [64]
+    uint32_t *planes; // quantised input: word (p*8+k)*nbp + b (p 0 = high, 1 = low), s at 16*nbp + b, nx at 17*nbp + b
+    uint32_t nbp;     // blocks of the input, rounded up to even
+    float *red;       // partial row sums [local row][warp of the slot]
     uint8_t *ring;
 };
 
@@ -296,17 +299,21 @@ __host__ __device__ constexpr uint32_t plane_bytes(uint32_t K) {
     return ((18u * (((K / 32) + 1) & ~1u) * 4u) + 127u) & ~127u;
 }
 
-__device__ __forceinline__ GemvSmem gemv_smem(uint8_t *smem, uint32_t K) {
+// Partial-sum area for n_loc local rows with slots `Upad` threads wide.
+__host__ __device__ constexpr uint32_t red_bytes_for(uint32_t Upad, uint32_t n_loc) {
+    return (((Upad > 32 ? Upad / 32 : 1u) * n_loc * 4u) + 127u) & ~127u;
+}
+
+__device__ __forceinline__ GemvSmem gemv_smem(uint8_t *smem, uint32_t K, uint32_t red_bytes) {
     GemvSmem g;
     g.full = reinterpret_cast<uint64_t *>(smem);
     g.done = reinterpret_cast<uint32_t *>(g.full + kMaxStages);
-    g.red = reinterpret_cast<float *>(smem + 256);    // [8][32]
-    g.out_tile = g.red + kRB * 32;                    // [512]
-    g.misc = g.out_tile + 512;                        // [64]
-    g.misc_u = reinterpret_cast<uint32_t *>(g.misc + 64);  // [64]
+    g.misc = reinterpret_cast<float *>(smem + 256);        // [64]
+    g.misc_u = reinterpret_cast<uint32_t *>(smem + 512);   // [64]
     g.planes = reinterpret_cast<uint32_t *>(smem + kHeaderBytes);
     g.nbp = ((K / 32) + 1) & ~1u;
-    g.ring = smem + kHeaderBytes + plane_bytes(K);
+    g.red = reinterpret_cast<float *>(smem + kHeaderBytes + plane_bytes(K));
+    g.ring = smem + kHeaderBytes + plane_bytes(K) + red_bytes;
     return g;
 }
 
@@ -356,14 +363,15 @@ struct RingState {
 
 // Called by lane 0 of every warp when it is done with stage rs.j: the last
 // warp to finish hands the slot to `refill`, which issues stage j + NS into
-// it (if such a stage exists).
+// it (if such a stage exists).  The proxy fence orders the warps' generic
+// reads of the slot before the bulk copy (async proxy) that overwrites it.
 template <class Refill>
 __device__ __forceinline__ void ring_release(const GemvSmem &sm, const RingState &rs, uint32_t nwarps,
                                              const Refill &refill) {
     __threadfence_block();
     if (atomicAdd(&sm.done[rs.slot], 1u) == nwarps - 1) {
         sm.done[rs.slot] = 0;
-        __threadfence_block();
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         refill(rs.j, rs.slot);
     }
 }
@@ -373,81 +381,107 @@ __device__ __forceinline__ void ring_advance(RingState &rs, uint32_t NS) {
     if (++rs.slot == NS) { rs.slot = 0; rs.par ^= 1u; }
 }
 
-// Quantise the input vector once per CTA into the shared plane area: a group
-// of 4 lanes per 32-block, 8 values per lane (RMSNorm applied when
-// IN_RMSNORM; `scale` is its factor).  Float -> int by adding 1.5*2^23
-// (exact round-to-nearest for |v| < 2^22).
+// Quantise the input once per CTA into the shared plane area, in one pass
+// over x: a group of 4 lanes per 32-block, 8 values per lane, and up to 4
+// blocks per thread loaded before any is used so that their L2 round trips
+// overlap.  With RMSNorm (rms_norm, norm.c:7-16) the values are multiplied by
+// the norm weight here; the 1/rms factor is a common scale of every block, so
+// it is applied to the block scales afterwards instead of to the values, and
+// x is read once.  Float -> int by adding 1.5*2^23 (exact round-to-nearest
+// for |v| < 2^22).  Ends with a CTA barrier.  Returns the 1/rms factor
+// 1/sqrtf(sum(x^2)/K + eps) (IEEE division and square root; every thread
+// sums the warp partials in the same order), or 1 without the norm.
 template <int OFF>
-__device__ void build_planes(const GemvArgs &a, const GemvSmem &sm, uint32_t tid, uint32_t NC, float scale) {
+__device__ float build_planes(const GemvArgs &a, const GemvSmem &sm, uint32_t tid, uint32_t NC) {
+    constexpr int kPass = 4;
     const bool norm = a.norm != 0;
     const uint32_t nb = a.K >> 5, nbp = sm.nbp;
-    const uint32_t q = tid & 3;
-    for (uint32_t b = tid >> 2; b < ((nb + 7) & ~7u); b += NC >> 2) {  // whole warps iterate together
-        const bool on = b < nb;
-        float v[8];
-        const uint32_t c = b * 32 + q * 8;
+    const uint32_t q = tid & 3, lane = tid & 31, warp = tid >> 5;
+    const uint32_t per = NC >> 2;  // blocks per pass
+    float ss = 0.f;
+    for (uint32_t b0 = 0; b0 < nb; b0 += kPass * per) {
+        float v[kPass][8], wn[kPass][8];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (on) {
-                t = __ldcg(reinterpret_cast<const float4 *>(a.x + c + 4 * h));  // written by other CTAs
-                if (norm) {
-                    const float4 w = *reinterpret_cast<const float4 *>(a.norm_w + c + 4 * h);
-                    t.x = __fmul_rn(__fmul_rn(t.x, w.x), scale);
-                    t.y = __fmul_rn(__fmul_rn(t.y, w.y), scale);
-                    t.z = __fmul_rn(__fmul_rn(t.z, w.z), scale);
-                    t.w = __fmul_rn(__fmul_rn(t.w, w.w), scale);
+        for (int p = 0; p < kPass; ++p) {
+            const uint32_t b = b0 + p * per + (tid >> 2);
+            const bool on = b < nb;
+            const uint32_t c = b * 32 + q * 8;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                float4 t = make_float4(0.f, 0.f, 0.f, 0.f), u = make_float4(1.f, 1.f, 1.f, 1.f);
+                if (on) {
+                    t = __ldcg(reinterpret_cast<const float4 *>(a.x + c + 4 * h));  // written by other CTAs
+                    if (norm) u = __ldg(reinterpret_cast<const float4 *>(a.norm_w + c + 4 * h));
+                }
+                v[p][4 * h] = t.x; v[p][4 * h + 1] = t.y; v[p][4 * h + 2] = t.z; v[p][4 * h + 3] = t.w;
+                wn[p][4 * h] = u.x; wn[p][4 * h + 1] = u.y; wn[p][4 * h + 2] = u.z; wn[p][4 * h + 3] = u.w;
+            }
+        }
+#pragma unroll
+        for (int p = 0; p < kPass; ++p) {
+            if (b0 + p * per >= nb) break;  // uniform over the CTA
+            const uint32_t b = b0 + p * per + (tid >> 2);
+            const bool on = b < nb;
+            if (norm) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    ss = fmaf(v[p][j], v[p][j], ss);
+                    v[p][j] = __fmul_rn(v[p][j], wn[p][j]);
                 }
             }
-            v[4 * h] = t.x; v[4 * h + 1] = t.y; v[4 * h + 2] = t.z; v[4 * h + 3] = t.w;
-        }
-        float m = 0.f, chk = 0.f;
+            float m = 0.f, chk = 0.f;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            m = fmaxf(m, fabsf(v[j]));
-            chk += v[j];  // NaN / inf propagate here (fmaxf would drop NaN)
-        }
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-        const bool bad = !isfinite(chk) || !isfinite(m);
-        const float inv = m > 1e-30f && !bad ? (float)kXMax / m : 0.f;
-        int xi[8], sum = 0;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            xi[j] = __float_as_int(fmaf(v[j], inv, kMagic)) - kMagicBits;
-            sum += xi[j];
-        }
-        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-        if (on) {
-#pragma unroll
-            for (int w = 0; w < 2; ++w) {
-                const int *x4 = xi + 4 * w;
-                // |xi| <= 32767: byte 0 is the low plane, byte 1 the signed high plane
-                const uint32_t t01 = __byte_perm(x4[0], x4[1], 0x5140), t23 = __byte_perm(x4[2], x4[3], 0x5140);
-                const uint32_t lo = __byte_perm(t01, t23, 0x5410), hi = __byte_perm(t01, t23, 0x7632);
-                const uint32_t k = 2 * q + w;
-                sm.planes[(0 * 8 + k) * nbp + b] = hi;
-                sm.planes[(1 * 8 + k) * nbp + b] = lo;
+            for (int j = 0; j < 8; ++j) {
+                m = fmaxf(m, fabsf(v[p][j]));
+                chk += v[p][j];  // NaN / inf propagate here (fmaxf would drop NaN)
             }
-            if (q == 0) {
-                sm.planes[16 * nbp + b] = __float_as_uint(bad ? __int_as_float(0x7fc00000)
-                                                              : (m > 1e-30f ? m * (1.0f / (float)kXMax) : 0.f));
-                sm.planes[17 * nbp + b] = __float_as_uint((float)(-OFF) * (float)sum);
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+            const bool bad = !isfinite(chk) || !isfinite(m);
+            const float inv = m > 1e-30f && !bad ? (float)kXMax / m : 0.f;
+            int xi[8], sum = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                xi[j] = __float_as_int(fmaf(v[p][j], inv, kMagic)) - kMagicBits;
+                sum += xi[j];
+            }
+            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+            if (on) {
+#pragma unroll
+                for (int w = 0; w < 2; ++w) {
+                    const int *x4 = xi + 4 * w;
+                    // |xi| <= 32767: byte 0 is the low plane, byte 1 the signed high plane
+                    const uint32_t t01 = __byte_perm(x4[0], x4[1], 0x5140), t23 = __byte_perm(x4[2], x4[3], 0x5140);
+                    const uint32_t lo = __byte_perm(t01, t23, 0x5410), hi = __byte_perm(t01, t23, 0x7632);
+                    const uint32_t k = 2 * q + w;
+                    sm.planes[(0 * 8 + k) * nbp + b] = hi;
+                    sm.planes[(1 * 8 + k) * nbp + b] = lo;
+                }
+                if (q == 0) {
+                    sm.planes[16 * nbp + b] = __float_as_uint(bad ? __int_as_float(0x7fc00000)
+                                                                  : (m > 1e-30f ? m * (1.0f / (float)kXMax) : 0.f));
+                    sm.planes[17 * nbp + b] = __float_as_uint((float)(-OFF) * (float)sum);
+                }
             }
         }
     }
+    if (norm) {
+#pragma unroll
+        for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0) sm.misc[warp] = ss;
+    }
+    bar_sync(1, NC);
+    if (!norm) return 1.0f;
+    float t = 0.f;
+    for (uint32_t w = 0; w < (NC >> 5); ++w) t += sm.misc[w];
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)a.K), a.eps)));
 }
 
-// This thread's two input blocks (2u, 2u+1) from the plane area.
-__device__ __forceinline__ void load_planes(const GemvSmem &sm, uint32_t unit, bool active, XBlock &xa, XBlock &xb) {
+// This thread's two input blocks (2u, 2u+1) from the plane area, block
+// scales multiplied by `scale`.
+__device__ __forceinline__ void load_planes(const GemvSmem &sm, uint32_t unit, float scale, XBlock &xa, XBlock &xb) {
     const uint32_t nbp = sm.nbp, b = 2 * unit;
-    if (!active) {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) { xa.hi[k] = xa.lo[k] = xb.hi[k] = xb.lo[k] = 0; }
-        xa.s = xb.s = xa.nx = xb.nx = 0.f;
-        return;
-    }
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
         const uint2 h = *reinterpret_cast<const uint2 *>(sm.planes + (0 * 8 + k) * nbp + b);
@@ -457,39 +491,24 @@ __device__ __forceinline__ void load_planes(const GemvSmem &sm, uint32_t unit, b
     }
     const uint2 sv = *reinterpret_cast<const uint2 *>(sm.planes + 16 * nbp + b);
     const uint2 nv = *reinterpret_cast<const uint2 *>(sm.planes + 17 * nbp + b);
-    xa.s = __uint_as_float(sv.x); xb.s = __uint_as_float(sv.y);
+    xa.s = __fmul_rn(__uint_as_float(sv.x), scale);
+    xb.s = __fmul_rn(__uint_as_float(sv.y), scale);
     xa.nx = __uint_as_float(nv.x); xb.nx = __uint_as_float(nv.y);
 }
 
-// RMSNorm factor over a.x (rms_norm, norm.c:7-16):
-// 1/sqrtf(sum(x^2)/n + eps), IEEE division and square root.
-__device__ float rms_scale(const GemvArgs &a, const GemvSmem &sm, uint32_t tid, uint32_t NC) {
-    const uint32_t lane = tid & 31, warp = tid >> 5, NCW = NC >> 5;
-    float ss = 0.f;
-    for (uint32_t i = tid * 4; i < a.K; i += NC * 4) {
-        const float4 t = __ldcg(reinterpret_cast<const float4 *>(a.x + i));
-        ss = fmaf(t.x, t.x, ss);
-        ss = fmaf(t.y, t.y, ss);
-        ss = fmaf(t.z, t.z, ss);
-        ss = fmaf(t.w, t.w, ss);
-    }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if (lane == 0) sm.misc[warp] = ss;
-    bar_sync(1, NC);
-    if (warp == 0) {
-        float t = lane < NCW ? sm.misc[lane] : 0.f;
-#pragma unroll
-        for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-        if (lane == 0) sm.misc[32] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)a.K), a.eps)));
-    }
-    bar_sync(1, NC);
-    const float r = sm.misc[32];
-    bar_sync(1, NC);
-    return r;
+// RoPE of one adjacent pair (rope.c:37-43).
+__device__ __forceinline__ void rope_pair(float v0, float v1, float c, float s, float &r0, float &r1) {
+    r0 = __fsub_rn(__fmul_rn(v0, c), __fmul_rn(v1, s));
+    r1 = __fadd_rn(__fmul_rn(v0, s), __fmul_rn(v1, c));
 }
 
-// Consumers: returns false if a bounded wait failed (results then invalid).
+// One GEMV over this CTA's rows.  Returns false if a bounded wait failed
+// (results then invalid).
+//
+// Structure: prologue (input planes; epilogue operands fetched early), the
+// row loop (no CTA-wide barrier: each warp reduces its partial sums of a batch
+// of 8 rows per slot with shuffles and parks them in shared memory), one CTA
+// barrier, then the epilogue over all local rows.
 template <int QT, bool A4, class Refill>
 __device__ bool gemv_consume(const GemvArgs &a, const GemvSmem &sm, uint32_t tid, RingState &rs,
                              const Refill &refill) {
@@ -499,8 +518,8 @@ __device__ bool gemv_consume(const GemvArgs &a, const GemvSmem &sm, uint32_t tid
     const bool PAIRED = MODE == GM_SWIGLU;
     constexpr int BB = QTraits<QT>::BB;
     constexpr int OFF = QTraits<QT>::OFF;
-    // a.NC threads carry (slot, unit) work; the whole block takes part in the
-    // ring protocol, barriers and epilogues
+    constexpr uint32_t RPT = QTraits<QT>::RPT;
+    constexpr int RND = kRB / (int)RPT;  // rounds per reduction batch
     const uint32_t NC = blockDim.x, lane = tid & 31, warp = tid >> 5, NCW = NC >> 5;
     uint32_t rb, re;
     cta_rows(a.n_out, a.gran, rb, re);
@@ -508,163 +527,171 @@ __device__ bool gemv_consume(const GemvArgs &a, const GemvSmem &sm, uint32_t tid
     const uint32_t Upad = a.Upad, S = a.S, U = a.U;
     const uint32_t slot = tid / Upad, unit = tid % Upad;
     const uint32_t nb = a.K >> 5;
-    const bool active = tid < a.NC && slot < S && unit < U;
-    const bool two = active && (2 * unit + 1 < nb);
+    const bool active = slot < S && unit < U;
+    const uint32_t slot_c = min(slot, S - 1), unit_c = min(unit, U - 1);  // in-bounds for inactive threads
+    const bool two = 2 * unit_c + 1 < nb;
     const uint32_t G = Upad < 32 ? Upad : 32;
-    constexpr uint32_t RPT = QTraits<QT>::RPT;
+    const uint32_t Wg = Upad > 32 ? Upad >> 5 : 1u;  // warps per slot
+    const uint32_t wg = Upad > 32 ? warp % Wg : 0u;
     const uint32_t RS = RPT * S;  // local rows per round
 
     const bool prof = a.prof != nullptr && tid == 0;
-    unsigned long long t0 = prof ? gtime_ns() : 0ull, t_wait = 0ull;
-    const float scale = a.norm ? rms_scale(a, sm, tid, NC) : 1.0f;
-    build_planes<OFF>(a, sm, tid, NC, scale);
-    bar_sync(1, NC);
-    unsigned long long t1 = prof ? gtime_ns() : 0ull;
-    XBlock xa, xb;
-    load_planes(sm, unit, active, xa, xb);
+    const unsigned long long t0 = prof ? gtime_ns() : 0ull;
 
-    // One ring stage per round: stage k holds local rows [k*RS, (k+1)*RS).
-    const uint32_t n_rounds = (n_loc + RS - 1) / RS;
-    const uint32_t NS = a.NS, rbytes = a.row_bytes, sbytes = a.stage_bytes;
-    const uint32_t pos = MODE == GM_QKV ? __ldcg(&a.step[1]) : 0u;
-    bool ok = true;
-    float best_v = -INFINITY;
-    uint32_t best_i = 0xffffffffu;
-    // byte offset (inside a stage, before the alignment delta) of this
-    // thread's unit in each of its RPT rows; paired stages hold the gate rows
-    // in the first half and the up rows in the second, interleaved as
-    // local rows (gate, up, gate, up, ...)
-    uint32_t off[RPT];
-    bool up_half[RPT];
-    const uint32_t slot_c = min(slot, S - 1), unit_c = min(unit, U - 1);  // in-bounds for inactive threads
-#pragma unroll
-    for (uint32_t e = 0; e < RPT; ++e) {
-        const uint32_t ls = e * S + slot_c;
-        if (!PAIRED) {
-            off[e] = ls * rbytes + unit_c * (2 * BB);
-            up_half[e] = false;
-        } else {
-            off[e] = (ls >> 1) * rbytes + unit_c * (2 * BB) + ((ls & 1) ? sbytes / 2 : 0u);
-            up_half[e] = ls & 1;
+    // epilogue operands, fetched now so that their latency hides behind the loop
+    float pre_y = 0.f;
+    uint32_t pos = 0;
+    if (MODE == GM_RESID && tid < n_loc) pre_y = __ldcg(&a.y[rb + tid]);
+    if (MODE == GM_QKV) pos = __ldcg(&a.step[1]);
+
+    const float rscale = build_planes<OFF>(a, sm, tid, NC);
+    XBlock xa, xb;
+    load_planes(sm, unit_c, rscale, xa, xb);
+
+    float rc = 1.f, rsn = 0.f;  // GM_QKV: RoPE factors of this thread's first pair
+    const uint32_t half = a.head_dim >> 1;
+    if (MODE == GM_QKV && 2 * tid < n_loc) {
+        const uint32_t g = rb + 2 * tid;
+        if (g < a.n_q + a.n_kv) {
+            const uint32_t d = (g < a.n_q ? g : g - a.n_q) % a.head_dim;
+            rc = __ldg(&a.rope_cos[pos * half + d / 2]);
+            rsn = __ldg(&a.rope_sin[pos * half + d / 2]);
         }
     }
-    // low 32 bits of the first source byte of the current stage (gate / up),
-    // advanced per stage; only the value mod 16 (the alignment delta) is used
-    uint32_t src_a = (uint32_t)(reinterpret_cast<uintptr_t>(a.w) + (uint64_t)rb * rbytes);
-    uint32_t src_b = PAIRED ? (uint32_t)(reinterpret_cast<uintptr_t>(a.w2) + (uint64_t)rb * rbytes) : 0u;
-    const uint32_t src_step = PAIRED ? (RS / 2) * rbytes : RS * rbytes;
-    const uint8_t *ring = sm.ring;
+    const unsigned long long t1 = prof ? gtime_ns() : 0ull;
 
-    for (uint32_t r0 = 0; r0 < n_rounds; r0 += kRB / RPT) {
+    // One ring stage per round: local stage k holds local rows [k*RS, (k+1)*RS).
+    const uint32_t n_rounds = (n_loc + RS - 1) / RS;
+    const uint32_t NS = a.NS, rbytes = a.row_bytes, sbytes = a.stage_bytes;
+    // Stage k's rows start (src(k) & 15) bytes into its slot, src(k) = base +
+    // k * sstep; the offset is the same for every stage unless sstep % 16 != 0.
+    const uintptr_t base_a = reinterpret_cast<uintptr_t>(a.w) + (uint64_t)rb * rbytes;
+    const uintptr_t base_b = PAIRED ? reinterpret_cast<uintptr_t>(a.w2) + (uint64_t)rb * rbytes : 0;
+    const uint32_t sstep = PAIRED ? (RS / 2) * rbytes : RS * rbytes;
+    const bool var_delta = (sstep & 15u) != 0;
+    // byte offset inside a stage of this thread's unit in each of its RPT
+    // local rows slot*RPT + e; paired stages hold the gate rows in the first
+    // half and the up rows in the second, local rows (gate, up, gate, up, ...)
+    uint32_t off[RPT], cur[RPT];
+    bool upper[RPT];
+#pragma unroll
+    for (uint32_t e = 0; e < RPT; ++e) {
+        const uint32_t ls = slot_c * RPT + e;
+        if (!PAIRED) {
+            off[e] = ls * rbytes + unit_c * (2 * BB);
+            upper[e] = false;
+        } else {
+            off[e] = (ls >> 1) * rbytes + unit_c * (2 * BB) + ((ls & 1) ? sbytes / 2 : 0u);
+            upper[e] = ls & 1;
+        }
+    }
+    auto set_delta = [&](uint32_t k) {
+        const uint32_t da = (uint32_t)(base_a + (uint64_t)k * sstep) & 15u;
+        const uint32_t db = (uint32_t)(base_b + (uint64_t)k * sstep) & 15u;
+#pragma unroll
+        for (uint32_t e = 0; e < RPT; ++e) cur[e] = off[e] + (upper[e] ? db : da);
+    };
+    set_delta(0);
+
+    bool ok = true;
+    unsigned long long t_wait = 0ull;
+    if (prof && n_rounds) {  // time until the phase's first stage has landed
+        const unsigned long long w0 = gtime_ns();
+        ok = mbar_wait(&sm.full[rs.slot], rs.par, a.err, ERR_WAIT_FULL);
+        t_wait = gtime_ns() - w0;
+    }
+    const uint8_t *ring = sm.ring;
+    for (uint32_t r0 = 0; r0 < n_rounds; r0 += RND) {
         float acc[kRB];
 #pragma unroll
-        for (int jj = 0; jj < kRB / (int)RPT; ++jj) {
-#pragma unroll
-            for (uint32_t e = 0; e < RPT; ++e) acc[RPT * jj + e] = 0.f;
+        for (int jj = 0; jj < RND; ++jj) {
             const uint32_t r = r0 + jj;
             if (r < n_rounds) {
-                if (prof) {
-                    const unsigned long long w0 = gtime_ns();
-                    if (ok) ok = mbar_wait(&sm.full[rs.slot], rs.par, a.err, ERR_WAIT_FULL);
-                    t_wait += gtime_ns() - w0;
-                } else if (ok) {
-                    ok = mbar_wait(&sm.full[rs.slot], rs.par, a.err, ERR_WAIT_FULL);
-                }
+                if (ok) ok = mbar_wait(&sm.full[rs.slot], rs.par, a.err, ERR_WAIT_FULL);
+                if (var_delta) set_delta(r);
                 // every thread computes (inactive ones on clamped, in-bounds
                 // addresses) so the body has no divergent branch
                 const uint8_t *sb = ring + rs.slot * sbytes;
-                float d[RPT];
 #pragma unroll
                 for (uint32_t e = 0; e < RPT; ++e) {
-                    const uint32_t delta = up_half[e] ? (src_b & 15u) : (src_a & 15u);
-                    d[e] = unit_dot<QT, A4>(sb + off[e] + delta, xa, xb, two);
+                    const float d = unit_dot<QT, A4>(sb + cur[e], xa, xb, two);
+                    acc[RPT * jj + e] = active ? d : 0.f;
                 }
-                const uint32_t lr = r * RS + slot;
-#pragma unroll
-                for (uint32_t e = 0; e < RPT; ++e) acc[RPT * jj + e] = (active && lr + e * S < n_loc) ? d[e] : 0.f;
                 __syncwarp();
                 if (lane == 0) ring_release(sm, rs, NCW, refill);
-                src_a += src_step;
-                src_b += src_step;
                 ring_advance(rs, NS);
+            } else {
+#pragma unroll
+                for (uint32_t e = 0; e < RPT; ++e) acc[RPT * jj + e] = 0.f;
             }
         }
-
-        // ---- reduce: acc[i] belongs to local row (r0 + i/RPT)*RS + (i%RPT)*S + slot,
-        //      i.e. out_tile index (i/RPT)*RS + (i%RPT)*S + slot
+        // acc[i] belongs to local row (r0 + i/RPT)*RS + slot*RPT + i%RPT; the
+        // reduce-scatter leaves row jj8 of the batch (summed over this warp's
+        // lanes of the slot) on every (G/8)-th lane
         uint32_t jj8;
         const float v = reduce8(acc, lane, G, jj8);
-        const uint32_t tpos = (jj8 / RPT) * RS + (jj8 % RPT) * S;
-        if (Upad <= 32) {
-            if ((lane & ((G >> 3) - 1)) == 0 && slot < S) sm.out_tile[tpos + slot] = v;
-        } else {
-            if ((lane & 3) == 0) sm.red[jj8 * 32 + warp] = v;
-            bar_sync(1, NC);
-            const uint32_t W = Upad >> 5;
-            if (tid < kRB * S) {
-                const uint32_t j = tid % kRB, s = tid / kRB;
-                float t = 0.f;
-                for (uint32_t w = 0; w < W; ++w) t += sm.red[j * 32 + s * W + w];
-                sm.out_tile[(j / RPT) * RS + (j % RPT) * S + s] = t;
-            }
-        }
-        bar_sync(1, NC);
-
-        // ---- epilogue on local rows [r0*RS, r0*RS + cnt)
-        const uint32_t l0 = r0 * RS;  // even: RS * (kRB / RPT) is even
-        const uint32_t cnt = min((uint32_t)(kRB / RPT) * RS, n_loc - l0);
-        if (ok) {
-            if (MODE == GM_STORE || MODE == GM_RESID || MODE == GM_LOGITS) {
-                for (uint32_t i = tid; i < cnt; i += NC) {
-                    const uint32_t g = rb + l0 + i;
-                    const float t = sm.out_tile[i];
-                    if (MODE == GM_STORE) a.y[g] = t;
-                    if (MODE == GM_RESID) a.y[g] = __fadd_rn(__ldcg(&a.y[g]), t);
-                    if (MODE == GM_LOGITS) {
-                        a.y[g] = t;
-                        if (t > best_v || (t == best_v && g < best_i)) { best_v = t; best_i = g; }
-                    }
-                }
-            } else if (MODE == GM_SWIGLU) {
-                for (uint32_t i = tid; 2 * i < cnt; i += NC) {
-                    const uint32_t p = rb + (l0 >> 1) + i;
-                    a.y[p] = __fmul_rn(silu_ref(sm.out_tile[2 * i]), sm.out_tile[2 * i + 1]);
-                }
-            } else if (MODE == GM_QKV) {
-                const uint32_t half = a.head_dim >> 1;
-                for (uint32_t i = tid; 2 * i < cnt; i += NC) {
-                    const uint32_t g = rb + l0 + 2 * i;
-                    const float v0 = sm.out_tile[2 * i], v1 = sm.out_tile[2 * i + 1];
-                    if (g < a.n_q + a.n_kv) {
-                        const uint32_t gg = g < a.n_q ? g : g - a.n_q;
-                        const uint32_t d = gg % a.head_dim;
-                        const float c = a.rope_cos[pos * half + d / 2], s = a.rope_sin[pos * half + d / 2];
-                        // rope.c:37-43 (adjacent pairs)
-                        const float r0v = __fsub_rn(__fmul_rn(v0, c), __fmul_rn(v1, s));
-                        const float r1v = __fadd_rn(__fmul_rn(v0, s), __fmul_rn(v1, c));
-                        if (g < a.n_q) {
-                            a.q_out[g] = r0v;
-                            a.q_out[g + 1] = r1v;
-                        } else {
-                            const uint32_t h = gg / a.head_dim;
-                            float *dst = a.kcache + ((size_t)h * a.kv_ctx + pos) * a.head_dim + d;
-                            dst[0] = r0v;
-                            dst[1] = r1v;
-                        }
-                    } else {
-                        const uint32_t gv = g - a.n_q - a.n_kv;
-                        const uint32_t h = gv / a.head_dim, d = gv % a.head_dim;
-                        float *dst = a.vcache + ((size_t)h * a.kv_ctx + pos) * a.head_dim + d;
-                        dst[0] = v0;
-                        dst[1] = v1;
-                    }
-                }
-            }
-        }
-        bar_sync(1, NC);
+        const uint32_t lrow = (r0 + jj8 / RPT) * RS + slot * RPT + jj8 % RPT;
+        if ((lane & ((G >> 3) - 1)) == 0 && slot < S && lrow < n_loc) sm.red[lrow * Wg + wg] = v;
     }
 
     const unsigned long long t2 = prof ? gtime_ns() : 0ull;
+    bar_sync(1, NC);  // every partial sum is parked
+
+    // ---- epilogue over all local rows
+    float best_v = -INFINITY;
+    uint32_t best_i = 0xffffffffu;
+    auto row_sum = [&](uint32_t i) {
+        float t = 0.f;
+        for (uint32_t w = 0; w < Wg; ++w) t += sm.red[i * Wg + w];
+        return t;
+    };
+    if (ok) {
+        if (MODE == GM_STORE || MODE == GM_RESID || MODE == GM_LOGITS) {
+            for (uint32_t i = tid; i < n_loc; i += NC) {
+                const uint32_t g = rb + i;
+                const float t = row_sum(i);
+                if (MODE == GM_STORE) a.y[g] = t;
+                if (MODE == GM_RESID) a.y[g] = __fadd_rn(i == tid ? pre_y : __ldcg(&a.y[g]), t);
+                if (MODE == GM_LOGITS) {
+                    a.y[g] = t;
+                    const uint32_t gi = a.idx_base + g;
+                    if (t > best_v || (t == best_v && gi < best_i)) { best_v = t; best_i = gi; }
+                }
+            }
+        } else if (MODE == GM_SWIGLU) {
+            for (uint32_t i = tid; 2 * i < n_loc; i += NC)
+                a.y[rb + i] = __fmul_rn(silu_ref(row_sum(2 * i)), row_sum(2 * i + 1));
+        } else if (MODE == GM_QKV) {
+            for (uint32_t i = tid; 2 * i < n_loc; i += NC) {
+                const uint32_t g = rb + 2 * i;
+                const float v0 = row_sum(2 * i), v1 = row_sum(2 * i + 1);
+                if (g < a.n_q + a.n_kv) {
+                    const uint32_t gg = g < a.n_q ? g : g - a.n_q;
+                    const uint32_t d = gg % a.head_dim;
+                    const float c = i == tid ? rc : __ldg(&a.rope_cos[pos * half + d / 2]);
+                    const float sn = i == tid ? rsn : __ldg(&a.rope_sin[pos * half + d / 2]);
+                    float r0v, r1v;
+                    rope_pair(v0, v1, c, sn, r0v, r1v);
+                    if (g < a.n_q) {
+                        a.q_out[g] = r0v;
+                        a.q_out[g + 1] = r1v;
+                    } else {
+                        const uint32_t h = gg / a.head_dim;
+                        float *dst = a.kcache + ((size_t)h * a.kv_ctx + pos) * a.head_dim + d;
+                        dst[0] = r0v;
+                        dst[1] = r1v;
+                    }
+                } else {
+                    const uint32_t gv = g - a.n_q - a.n_kv;
+                    const uint32_t h = gv / a.head_dim, d = gv % a.head_dim;
+                    float *dst = a.vcache + ((size_t)h * a.kv_ctx + pos) * a.head_dim + d;
+                    dst[0] = v0;
+                    dst[1] = v1;
+                }
+            }
+        }
+    }
+
     if (MODE == GM_LOGITS) {
         // CTA argmax, then the last CTA to finish reduces the per-CTA results
         // (sampler.c:28-32: the lowest index wins among equal maxima)
@@ -711,14 +738,19 @@ __device__ bool gemv_consume(const GemvArgs &a, const GemvSmem &sm, uint32_t tid
                 bi = sm.misc_u[0];
                 for (uint32_t w = 1; w < NCW; ++w)
                     if (sm.misc[w] > bv || (sm.misc[w] == bv && sm.misc_u[w] < bi)) { bv = sm.misc[w]; bi = sm.misc_u[w]; }
-                // every logit NaN: the reference keeps index 0
-                const uint32_t nxt = bi == 0xffffffffu ? 0u : bi;
-                *a.out_token = nxt;
-                if (a.hist) {  // feed the greedy token into the next step
-                    const uint32_t pos = __ldcg(&a.step_rw[1]);
-                    a.hist[pos] = nxt;
-                    a.step_rw[0] = nxt;
-                    a.step_rw[1] = pos + 1;
+                if (a.tp_cand) {  // the ranks' candidates are combined after a global barrier
+                    a.tp_cand[0] = bv;
+                    reinterpret_cast<uint32_t *>(a.tp_cand)[1] = bi;
+                } else {
+                    // every logit NaN: the reference keeps index 0
+                    const uint32_t nxt = bi == 0xffffffffu ? 0u : bi;
+                    *a.out_token = nxt;
+                    if (a.hist) {  // feed the greedy token into the next step
+                        const uint32_t p = __ldcg(&a.step_rw[1]);
+                        a.hist[p] = nxt;
+                        a.step_rw[0] = nxt;
+                        a.step_rw[1] = p + 1;
+                    }
                 }
                 *a.ticket = 0;
             }
@@ -750,7 +782,7 @@ template <int QT, bool A4>
 __global__ void __launch_bounds__(kMaxConsumers, 1) gemv_kernel(const __grid_constant__ GemvArgs a) {
     const bool PAIRED = a.mode == GM_SWIGLU;
     extern __shared__ __align__(128) uint8_t smem[];
-    const GemvSmem sm = gemv_smem(smem, a.K);
+    const GemvSmem sm = gemv_smem(smem, a.K, a.red_bytes);
     const uint32_t tid = threadIdx.x;
     uint32_t rb, re;
     cta_rows(a.n_out, a.gran, rb, re);

@@ -22,6 +22,7 @@
 #include "attention.cuh"
 #include "gemv.cuh"
 #include "gguf_reader.h"
+#include "tp_shard.h"
 #include "decode.cuh"
 #include "misc_kernels.cuh"
 
@@ -153,10 +154,16 @@ static bool plan_gemv(int qt, int mode, int sms, GemvLaunch &L) {
     }
     a.stage_bytes = stage;
     const uint32_t n_st = (max_loc + R - 1) / R;
-    uint32_t ns = std::max(2u, std::min((uint32_t)kMaxStages, (kRingBudget - plane_bytes(a.K)) / stage));
+    a.red_bytes = red_bytes_for(a.Upad, max_loc);
+    const uint32_t fixed = plane_bytes(a.K) + a.red_bytes;
+    if (fixed + kHeaderBytes + 1024 + stage + 128 > kMaxSmem) {
+        set_err("gemv: too many rows per CTA for the shared partial sums");
+        return false;
+    }
+    uint32_t ns = std::max(2u, std::min((uint32_t)kMaxStages, kRingBudget > fixed ? (kRingBudget - fixed) / stage : 1u));
     ns = std::max(1u, std::min(ns, n_st));
     if (const char *e = getenv("FWB_MAX_NS")) ns = std::max(1u, std::min(ns, (uint32_t)atoi(e)));
-    const uint32_t room = kMaxSmem - 1024 - plane_bytes(a.K);  // static shared memory stays below 1 KB
+    const uint32_t room = kMaxSmem - 1024 - fixed;  // static shared memory stays below 1 KB
     while (ns > 1 && kHeaderBytes + ns * stage + 128 > room) --ns;
     if (kHeaderBytes + ns * stage + 128 > room) { set_err("gemv: stage does not fit shared memory"); return false; }
     a.NS = ns;
@@ -165,7 +172,7 @@ static bool plan_gemv(int qt, int mode, int sms, GemvLaunch &L) {
     if (!L.fn) { set_err("gemv: unsupported quant type"); return false; }
     L.grid = dim3(grid);
     L.block = dim3(a.NC);
-    L.smem = kHeaderBytes + plane_bytes(a.K) + (size_t)ns * stage + 128;
+    L.smem = kHeaderBytes + fixed + (size_t)ns * stage + 128;
     L.weight_bytes = (uint64_t)a.n_out * a.row_bytes * (paired ? 2 : 1);
     return true;
 }
@@ -389,6 +396,15 @@ struct fwb_model {
     size_t dsmem = 0;
     uint32_t *sync = nullptr;
     std::vector<void *> allocs;
+    // tensor parallelism (world > 1): this rank's exchange buffer, every
+    // rank's mapping of it (peer[rank] = xbuf), barrier epochs
+    uint32_t rank = 0, world = 1;
+    uint8_t *xbuf = nullptr;
+    uint64_t xbytes = 0, x_part = 0, x_logits = 0;
+    uint8_t *peer[fwb::kMaxRanks] = {};
+    bool peer_mapped[fwb::kMaxRanks] = {};
+    unsigned long long *gbase = nullptr;
+    bool connected = false;
 };
 
 namespace fwb {
@@ -417,6 +433,8 @@ static bool check_mat(const GgufTensor *t, uint32_t rows, uint32_t cols, const c
 static void free_model(fwb_model *m) {
     if (!m) return;
     if (m->st) cudaStreamSynchronize(m->st);
+    for (uint32_t q = 0; q < kMaxRanks; ++q)
+        if (m->peer_mapped[q]) cudaIpcCloseMemHandle(m->peer[q]);
     if (m->exec) cudaGraphExecDestroy(m->exec);
     if (m->graph) cudaGraphDestroy(m->graph);
     for (void *p : m->allocs) cudaFree(p);
@@ -457,6 +475,9 @@ static bool load_model(fwb_model *m, const char *path, size_t max_ctx) {
     const uint32_t E = c.n_embd, F = c.n_ff, hd = c.head_dim, H = c.n_head, KV = c.n_head_kv;
     if (!attn_fn(hd, H / KV)) { set_err("head_dim / GQA group outside this build"); return false; }
     if (E % 32 || F % 32 || (H * hd) != E) { set_err("model widths outside this build"); return false; }
+    const uint32_t W = m->world, rk = m->rank;
+    if (W > 1 && !tp_check(c, W, err)) { set_err(err); return false; }
+    const uint32_t Hr = H / W, KVr = KV / W, Fr = F / W, Vr = c.n_vocab / W;
 
     // resolve tensors once
     const GgufTensor *te = m->gguf.find("token_embd.weight");
@@ -497,27 +518,53 @@ static bool load_model(fwb_model *m, const char *path, size_t max_ctx) {
         off = (off + bytes + 256 + 255) / 256 * 256;
         return o;
     };
-    struct Pl { const GgufTensor *t; uint64_t off; };
+    // (tensor parallelism: every tensor is this rank's slice, see tp_shard.h)
+    struct Pl { const GgufTensor *t; uint64_t off; ShardSpec sp; uint64_t bytes; };
     std::vector<Pl> plan;
-    const uint64_t o_embd = place(te->bytes);
-    plan.push_back({te, o_embd});
+    auto spec = [&](const GgufTensor *t, bool as_head) {
+        const uint32_t cols = (uint32_t)t->dims[0], rows = t->n_dims >= 2 ? (uint32_t)t->dims[1] : 1u;
+        return tp_shard_spec(c, t->name, rows, cols, rk, W, as_head);
+    };
+    auto add = [&](const GgufTensor *t, bool as_head) {
+        Pl e{t, 0, spec(t, as_head), 0};
+        e.bytes = tp_shard_bytes(*t, e.sp);
+        e.off = place(e.bytes);
+        plan.push_back(e);
+        return plan.back();
+    };
+    const uint64_t o_embd = add(te, false).off;
     uint64_t o_head = o_embd;
-    if (th != te) { o_head = place(th->bytes); plan.push_back({th, o_head}); }
+    uint64_t head_bytes = te->bytes;
+    if (th != te || W > 1) {
+        const Pl &e = add(th, true);
+        o_head = e.off;
+        head_bytes = e.bytes;
+    }
     uint64_t o_onorm = 0;
-    if (tn) { o_onorm = place(tn->bytes); plan.push_back({tn, o_onorm}); }
+    if (tn) o_onorm = add(tn, false).off;
     std::vector<uint64_t> lo(c.n_layer * 8);
     for (uint32_t l = 0; l < c.n_layer; ++l) {
         LT &t = lt[l];
-        const uint64_t oq = place(t.q->bytes + t.k->bytes + t.v->bytes);
-        plan.push_back({t.q, oq});
-        plan.push_back({t.k, oq + t.q->bytes});
-        plan.push_back({t.v, oq + t.q->bytes + t.k->bytes});
-        const uint64_t oo = place(t.o->bytes), og = place(t.g->bytes), ou = place(t.u->bytes),
-                       od = place(t.d->bytes), oan = place(t.an->bytes), ofn = place(t.fn->bytes);
-        plan.push_back({t.o, oo}); plan.push_back({t.g, og}); plan.push_back({t.u, ou});
-        plan.push_back({t.d, od}); plan.push_back({t.an, oan}); plan.push_back({t.fn, ofn});
+        Pl pq{t.q, 0, spec(t.q, false), 0}, pk{t.k, 0, spec(t.k, false), 0}, pv{t.v, 0, spec(t.v, false), 0};
+        pq.bytes = tp_shard_bytes(*t.q, pq.sp);
+        pk.bytes = tp_shard_bytes(*t.k, pk.sp);
+        pv.bytes = tp_shard_bytes(*t.v, pv.sp);
+        const uint64_t oq = place(pq.bytes + pk.bytes + pv.bytes);
+        pq.off = oq;
+        pk.off = oq + pq.bytes;
+        pv.off = oq + pq.bytes + pk.bytes;
+        plan.push_back(pq); plan.push_back(pk); plan.push_back(pv);
         uint64_t *L = &lo[l * 8];
-        L[0] = oq; L[1] = oo; L[2] = og; L[3] = ou; L[4] = od; L[5] = oan; L[6] = ofn;
+        L[0] = oq;
+        L[1] = add(t.o, false).off;
+        L[2] = add(t.g, false).off;
+        L[3] = add(t.u, false).off;
+        L[4] = add(t.d, false).off;
+        L[5] = add(t.an, false).off;
+        L[6] = add(t.fn, false).off;
+        for (size_t i = plan.size() - 9; i < plan.size(); ++i)
+            if (plan[i].t != t.an && plan[i].t != t.fn) m->weight_bytes += plan[i].bytes;
+        m->weight_bytes += t.an->bytes + t.fn->bytes;
     }
     const uint64_t arena_bytes = off + 256;
     if (!dalloc(m, (void **)&m->arena, arena_bytes)) return false;
@@ -539,8 +586,18 @@ static bool load_model(fwb_model *m, const char *path, size_t max_ctx) {
             cudaEventRecord(ev[1], m->st);
         }
         int flip = 0;
-        for (size_t i = 0; ok && i < plan.size(); ++i)
-            ok = upload(plan[i].t->data, m->arena + plan[i].off, plan[i].t->bytes, stage, ev, chunk, m->st, flip);
+        std::vector<uint8_t> shard;
+        for (size_t i = 0; ok && i < plan.size(); ++i) {
+            const Pl &e = plan[i];
+            const uint8_t *src = e.t->data;
+            if (e.bytes != e.t->bytes) {  // a slice: packed on the host first
+                shard.resize(e.bytes);
+                tp_extract(*e.t, e.sp, shard.data());
+                src = shard.data();
+            }
+            ok = upload(src, m->arena + e.off, e.bytes, stage, ev, chunk, m->st, flip);
+            if (ok && e.bytes != e.t->bytes && cudaStreamSynchronize(m->st) != cudaSuccess) ok = false;
+        }
         if (ok && cudaStreamSynchronize(m->st) != cudaSuccess) { set_err("upload failed"); ok = false; }
         for (int i = 0; i < 2; ++i) {
             if (stage[i]) cudaFreeHost(stage[i]);
@@ -561,37 +618,47 @@ static bool load_model(fwb_model *m, const char *path, size_t max_ctx) {
         return mm;
     };
     m->embd = mat(te, o_embd, c.n_vocab, E);
-    m->head = mat(th, o_head, c.n_vocab, E);
+    m->head = mat(th, o_head, Vr, E);
     m->out_norm = tn ? reinterpret_cast<const float *>(m->arena + o_onorm) : nullptr;
     m->layers.resize(c.n_layer);
     for (uint32_t l = 0; l < c.n_layer; ++l) {
         LT &t = lt[l];
         uint64_t *L = &lo[l * 8];
         LayerW &w = m->layers[l];
-        w.qkv = mat(t.q, L[0], (H + 2 * KV) * hd, E);
-        w.o = mat(t.o, L[1], E, H * hd);
-        w.gate = mat(t.g, L[2], F, E);
-        w.up = mat(t.u, L[3], F, E);
-        w.down = mat(t.d, L[4], E, F);
+        w.qkv = mat(t.q, L[0], (Hr + 2 * KVr) * hd, E);
+        w.o = mat(t.o, L[1], E, Hr * hd);
+        w.gate = mat(t.g, L[2], Fr, E);
+        w.up = mat(t.u, L[3], Fr, E);
+        w.down = mat(t.d, L[4], E, Fr);
         w.attn_norm = reinterpret_cast<const float *>(m->arena + L[5]);
         w.ffn_norm = reinterpret_cast<const float *>(m->arena + L[6]);
-        m->weight_bytes += t.q->bytes + t.k->bytes + t.v->bytes + t.o->bytes + t.g->bytes + t.u->bytes +
-                           t.d->bytes + t.an->bytes + t.fn->bytes;
     }
-    m->weight_bytes += th->bytes + (tn ? tn->bytes : 0) + m->embd.row_bytes;
+    m->weight_bytes += head_bytes + (tn ? tn->bytes : 0) + m->embd.row_bytes;
 
     // state
-    const size_t kvn = (size_t)c.n_layer * KV * m->kv_ctx * hd;
-    if (!dalloc(m, (void **)&m->x, E * 4) || !dalloc(m, (void **)&m->q, (size_t)H * hd * 4) ||
-        !dalloc(m, (void **)&m->att, (size_t)H * hd * 4) || !dalloc(m, (void **)&m->h, (size_t)F * 4) ||
-        !dalloc(m, (void **)&m->logits, (size_t)c.n_vocab * 4) || !dalloc(m, (void **)&m->kc, kvn * 4) ||
+    const size_t kvn = (size_t)c.n_layer * KVr * m->kv_ctx * hd;
+    if (W > 1) {
+        // exchange buffer, mapped by every other rank: [0] cross-rank barrier
+        // counter (u64), [256] (value, index) argmax candidate, [512] two
+        // partial-output slots of n_embd floats, then this rank's logits
+        m->x_part = 512;
+        m->x_logits = (512 + 2ull * E * 4 + 255) / 256 * 256;
+        m->xbytes = m->x_logits + (uint64_t)Vr * 4 + 256;
+        if (!dalloc(m, (void **)&m->xbuf, m->xbytes) || !dalloc(m, (void **)&m->gbase, 64)) return false;
+        m->logits = reinterpret_cast<float *>(m->xbuf + m->x_logits);
+    } else if (!dalloc(m, (void **)&m->logits, (size_t)c.n_vocab * 4)) {
+        return false;
+    }
+    if (!dalloc(m, (void **)&m->x, E * 4) || !dalloc(m, (void **)&m->q, (size_t)Hr * hd * 4) ||
+        !dalloc(m, (void **)&m->att, (size_t)Hr * hd * 4) || !dalloc(m, (void **)&m->h, (size_t)Fr * 4) ||
+        !dalloc(m, (void **)&m->kc, kvn * 4) ||
         !dalloc(m, (void **)&m->vc, kvn * 4) ||
         !dalloc(m, (void **)&m->rope_cos, (size_t)m->kv_ctx * (hd / 2) * 4 + 4) ||
         !dalloc(m, (void **)&m->rope_sin, (size_t)m->kv_ctx * (hd / 2) * 4 + 4) ||
         !dalloc(m, (void **)&m->step, 64) || !dalloc(m, (void **)&m->err, 16) ||
         !dalloc(m, (void **)&m->hist, (size_t)m->kv_ctx * 4 + 4) ||
         !dalloc(m, (void **)&m->am_val, 4096 * 4) || !dalloc(m, (void **)&m->am_idx, 4096 * 4) ||
-        !dalloc(m, (void **)&m->am_ticket, 64) || !dalloc(m, (void **)&m->attn_ticket, 4 * KV + 64))
+        !dalloc(m, (void **)&m->am_ticket, 64) || !dalloc(m, (void **)&m->attn_ticket, 4 * KVr + 64))
         return false;
     CK(cudaMallocHost(&m->h_io, 64));
     CK(cudaMallocHost(&m->h_logits, (size_t)c.n_vocab * 4));
@@ -609,12 +676,14 @@ static bool load_model(fwb_model *m, const char *path, size_t max_ctx) {
         CK(cudaMemcpy(m->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
         CK(cudaMemcpy(m->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
     }
-    return build_steps(m);
+    return W > 1 ? true : build_steps(m);  // tensor parallel: after fwb_tp_connect
 }
 
+// Splits per KV head: one work item per CTA of the persistent kernel
+// (n_kv * splits <= number of SMs), so the attention phase is one wave.
 static uint32_t attn_splits(const fwb_model *m) {
-    const uint32_t KV = m->cfg.n_head_kv;
-    uint32_t s = (2u * m->sms + KV - 1) / KV;
+    const uint32_t KV = m->cfg.n_head_kv / m->world;
+    uint32_t s = std::min<uint32_t>(kMaxSplits, std::max(1u, (uint32_t)m->sms / KV));
     s = std::min(s, std::max(1u, m->kv_ctx / 16));
     return std::max(1u, s);
 }
@@ -622,7 +691,26 @@ static uint32_t attn_splits(const fwb_model *m) {
 static bool build_steps(fwb_model *m) {
     const ModelConfig &c = m->cfg;
     const uint32_t E = c.n_embd, F = c.n_ff, hd = c.head_dim, H = c.n_head, KV = c.n_head_kv;
-    const size_t layer_kv = (size_t)KV * m->kv_ctx * hd;
+    // per rank under tensor parallelism (world 1: the whole model)
+    const uint32_t W = m->world, Hr = H / W, KVr = KV / W, Fr = F / W, Vr = c.n_vocab / W;
+    const size_t layer_kv = (size_t)KVr * m->kv_ctx * hd;
+    uint32_t n_ar = 0;  // all-reduces so far (their partial slots alternate)
+    // sum of every rank's partial output into x, after a cross-rank barrier
+    auto allreduce_step = [&](const std::string &name) {
+        Step s;
+        s.name = name;
+        s.phase.kind = PH_ALLREDUCE;
+        s.phase.gsync = 1;
+        s.phase.ar.x = m->x;
+        s.phase.ar.n = E;
+        s.phase.ar.world = W;
+        for (uint32_t q = 0; q < W; ++q)
+            s.phase.ar.part[q] = reinterpret_cast<const float *>(m->peer[q] + m->x_part + (uint64_t)(n_ar & 1) * E * 4);
+        s.run = [](cudaStream_t, bool) { return cudaErrorNotSupported; };
+        m->steps.push_back(std::move(s));
+        ++n_ar;
+    };
+    auto part_out = [&]() { return reinterpret_cast<float *>(m->xbuf + m->x_part + (uint64_t)(n_ar & 1) * E * 4); };
     m->steps.clear();
 
     {  // embedding
@@ -682,15 +770,15 @@ static bool build_steps(fwb_model *m) {
     };
 
     const uint32_t nsplit = attn_splits(m);
-    if (!dalloc(m, (void **)&m->attn_part, (size_t)KV * nsplit * (H / KV) * (hd + 2) * 4)) return false;
+    if (!dalloc(m, (void **)&m->attn_part, (size_t)KVr * nsplit * (H / KV) * (hd + 2) * 4)) return false;
     const void *afn = attn_fn(hd, H / KV);
 
     for (uint32_t l = 0; l < c.n_layer; ++l) {
         const LayerW &w = m->layers[l];
         float *kc = m->kc + l * layer_kv, *vc = m->vc + l * layer_kv;
         GemvArgs ex{};
-        ex.n_q = H * hd;
-        ex.n_kv = KV * hd;
+        ex.n_q = Hr * hd;
+        ex.n_kv = KVr * hd;
         ex.head_dim = hd;
         ex.kv_ctx = m->kv_ctx;
         ex.rope_cos = m->rope_cos;
@@ -717,24 +805,38 @@ static bool build_steps(fwb_model *m) {
             a.step = m->step;
             a.err = m->err;
             s.bytes = 0;  // KV bytes depend on pos; accounted separately
-            a.n_kv = KV;
+            a.n_kv = KVr;
             s.phase.kind = PH_ATTN;
             s.phase.hd = hd;
             s.phase.gq = H / KV;
             s.phase.at = a;
             // the persistent kernel runs one (KV head, split) item per CTA
-            s.phase.at.n_split = std::max(1u, std::min(nsplit, (uint32_t)m->sms / KV));
-            s.run = [a, afn, KV, nsplit](cudaStream_t st, bool pdl) {
+            s.phase.at.n_split = std::max(1u, std::min(nsplit, (uint32_t)m->sms / KVr));
+            s.run = [a, afn, KVr, nsplit](cudaStream_t st, bool pdl) {
                 AttnArgs aa = a;
                 void *args[] = {&aa};
-                return launch_ex(afn, dim3(KV, nsplit), dim3(kAttnWarps * 32), 0, st, args, pdl);
+                return launch_ex(afn, dim3(KVr, nsplit), dim3(kAttnWarps * 32), 0, st, args, pdl);
             };
             m->steps.push_back(std::move(s));
         }
-        if (!gemv_step(p + "o_proj_resid", GM_RESID, w.o, nullptr, E, m->att, nullptr, m->x, GemvArgs{})) return false;
-        if (!gemv_step(p + "gate_up_swiglu", GM_SWIGLU, w.gate, &w.up, F, m->x, w.ffn_norm, m->h, GemvArgs{}))
+        if (W == 1) {
+            if (!gemv_step(p + "o_proj_resid", GM_RESID, w.o, nullptr, E, m->att, nullptr, m->x, GemvArgs{}))
+                return false;
+        } else {  // this rank's heads' share of o-proj, then the all-reduce into x
+            if (!gemv_step(p + "o_proj_part", GM_STORE, w.o, nullptr, E, m->att, nullptr, part_out(), GemvArgs{}))
+                return false;
+            allreduce_step(p + "o_proj_allreduce");
+        }
+        if (!gemv_step(p + "gate_up_swiglu", GM_SWIGLU, w.gate, &w.up, Fr, m->x, w.ffn_norm, m->h, GemvArgs{}))
             return false;
-        if (!gemv_step(p + "down_resid", GM_RESID, w.down, nullptr, E, m->h, nullptr, m->x, GemvArgs{})) return false;
+        if (W == 1) {
+            if (!gemv_step(p + "down_resid", GM_RESID, w.down, nullptr, E, m->h, nullptr, m->x, GemvArgs{}))
+                return false;
+        } else {
+            if (!gemv_step(p + "down_part", GM_STORE, w.down, nullptr, E, m->h, nullptr, part_out(), GemvArgs{}))
+                return false;
+            allreduce_step(p + "down_allreduce");
+        }
     }
     {
         GemvArgs ex{};
@@ -744,13 +846,48 @@ static bool build_steps(fwb_model *m) {
         ex.out_token = m->step + 2;
         ex.step_rw = m->step;
         ex.hist = m->hist;
-        if (!gemv_step("lm_head_argmax", GM_LOGITS, m->head, nullptr, c.n_vocab, m->x, m->out_norm, m->logits, ex))
+        ex.idx_base = m->rank * Vr;
+        if (W > 1) ex.tp_cand = reinterpret_cast<float *>(m->xbuf + 256);
+        if (!gemv_step("lm_head_argmax", GM_LOGITS, m->head, nullptr, Vr, m->x, m->out_norm, m->logits, ex))
             return false;
+    }
+    if (W > 1) {  // the greedy token from every rank's candidate
+        Step s;
+        s.name = "tp_argmax";
+        s.phase.kind = PH_TPARGMAX;
+        s.phase.gsync = 1;
+        s.phase.am.world = W;
+        for (uint32_t q = 0; q < W; ++q) s.phase.am.cand[q] = reinterpret_cast<const float *>(m->peer[q] + 256);
+        s.phase.am.out_token = m->step + 2;
+        s.phase.am.step_rw = m->step;
+        s.phase.am.hist = m->hist;
+        s.run = [](cudaStream_t, bool) { return cudaErrorNotSupported; };
+        m->steps.push_back(std::move(s));
     }
     // The head GEMV needs a norm weight; a model without output_norm gets the
     // identity norm (transformer.c:355-357 copies x unnormalised): not supported.
     if (!m->out_norm) { set_err("output_norm.weight is required by this build"); return false; }
     return !m->persistent || build_decode(m);
+}
+
+// Bytes of the attention scratch of the persistent kernel (16 warps).
+template <int HD>
+static uint32_t attn_smem_bytes_hd(uint32_t gq) {
+    constexpr int NW = kDecodeThreads / 32;
+    switch (gq) {
+    case 1: return sizeof(AttnSmem<HD, 1, NW>);
+    case 2: return sizeof(AttnSmem<HD, 2, NW>);
+    case 4: return sizeof(AttnSmem<HD, 4, NW>);
+    default: return sizeof(AttnSmem<HD, 8, NW>);
+    }
+}
+static uint32_t attn_smem_bytes(uint32_t hd, uint32_t gq) {
+    switch (hd) {
+    case 32: return attn_smem_bytes_hd<32>(gq);
+    case 48: return attn_smem_bytes_hd<48>(gq);
+    case 64: return attn_smem_bytes_hd<64>(gq);
+    default: return attn_smem_bytes_hd<128>(gq);
+    }
 }
 
 // Phases of the persistent kernel: the Step list's work, with one ring
@@ -764,13 +901,15 @@ static bool build_decode(fwb_model *m) {
     for (const Phase &p : ph) {
         if (p.kind == PH_GEMV) {
             stage = std::max(stage, p.g.stage_bytes);
-            scratch = std::max(scratch, plane_bytes(p.g.K));
+            scratch = std::max(scratch, plane_bytes(p.g.K) + p.g.red_bytes);
         }
     }
     {  // attention scratch of the persistent kernel (16 warps)
         const uint32_t hd = m->cfg.head_dim, gq = m->cfg.n_head / m->cfg.n_head_kv;
         const uint32_t nw = kDecodeThreads / 32;
-        const uint32_t att = (nw * 32 + 2 * nw * gq + nw * gq * hd + kMaxSplits * gq + gq + 1) * 4;
+        // the layout itself, and a formula check that every member is covered
+        const uint32_t att = std::max<uint32_t>(attn_smem_bytes(hd, gq),
+                                                (nw * 32 + 3 * nw * gq + nw * gq * hd + 2 * kMaxSplits * gq + 2 * gq + 1) * 4);
         scratch = std::max(scratch, (att + 127) / 128 * 128);
     }
     cudaFuncAttributes fa;
@@ -837,9 +976,20 @@ static bool build_decode(fwb_model *m) {
     d.sync = m->sync;
     d.err = m->err;
     d.n_st_cta = d_nst;
+    d.world = m->world;
+    d.gbase = m->gbase;
+    d.n_gsync = 0;
+    for (const Phase &p : ph) d.n_gsync += p.gsync;
+    if (m->world > 1) {  // [0] is this rank's own counter
+        d.gcount[0] = reinterpret_cast<unsigned long long *>(m->xbuf);
+        for (uint32_t q = 0, k = 1; q < m->world; ++q)
+            if (q != m->rank) d.gcount[k++] = reinterpret_cast<unsigned long long *>(m->peer[q]);
+    }
     const char *tr = getenv("FWB_TRACE");
     if (tr && *tr == '1') {
-        if (!dalloc(m, (void **)&d.trace, (2 * n_ph + 1) * 8)) return false;
+        if (!dalloc(m, (void **)&d.trace, (2 * n_ph + 1) * 8) ||
+            !dalloc(m, (void **)&d.trace_cta, (size_t)n_ph * G * 8))
+            return false;
     }
     m->dsmem = kHeaderBytes + scratch + (size_t)ns * stage + 128 + tab_bytes;
     CK(cudaFuncSetAttribute((const void *)decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->dsmem));
@@ -920,6 +1070,7 @@ static bool finish(fwb_model *m) {
 }
 
 static bool set_step(fwb_model *m, uint32_t tok, size_t pos) {
+    if (m->world > 1 && !m->connected) { set_err("tensor parallel model: call fwb_tp_connect first"); return false; }
     if (pos >= m->kv_ctx) { set_err("transformer_forward: position exceeds KV cache"); return false; }
     if (tok >= m->cfg.n_vocab) { set_err("transformer_forward: token ID out of range"); return false; }
     m->h_io[0] = tok;
@@ -1002,27 +1153,102 @@ int quant_dequant_dev(const void *d_weights, size_t weights_size, uint32_t ggml_
     return 0;
 }
 
-fwb_model_t *fwb_model_open(const char *path, size_t max_ctx, int device) {
+static fwb_model *open_model(const char *path, size_t max_ctx, int device, int rank, int world) {
     g_err.clear();
     if (!path) { set_err("null path"); return nullptr; }
+    if (world < 1 || world > (int)kMaxRanks || rank < 0 || rank >= world) {
+        set_err("tensor parallel: rank / world out of range (1 to 8 ranks)");
+        return nullptr;
+    }
     if (cudaSetDevice(device) != cudaSuccess) { set_err("cudaSetDevice failed"); return nullptr; }
     fwb_model *m = new fwb_model();
     m->dev = device;
     m->sms = num_sms(device);
+    m->rank = (uint32_t)rank;
+    m->world = (uint32_t)world;
     const char *ng = getenv("FWB_NO_GRAPH");
     const char *np = getenv("FWB_NO_PDL");
     m->use_graph = !(ng && *ng == '1');
     m->use_pdl = !(np && *np == '1');
     const char *mk = getenv("FWB_KERNEL_PER_PHASE");
     m->persistent = !(mk && *mk == '1');
-    if (cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking) != cudaSuccess || !set_smem_attrs(device) ||
-        !load_model(m, path, max_ctx) || (m->use_graph && !capture_graph(m))) {
+    bool ok = cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking) == cudaSuccess && set_smem_attrs(device);
+    if (ok && world > 1 && !m->persistent) {
+        set_err("tensor parallelism runs in the persistent decode kernel only (unset FWB_KERNEL_PER_PHASE)");
+        ok = false;
+    }
+    // tensor parallel: the step is built once the peers are mapped (fwb_tp_connect)
+    ok = ok && load_model(m, path, max_ctx) && (world > 1 || !m->use_graph || capture_graph(m));
+    if (!ok) {
         std::string e = g_err;
         free_model(m);
         set_err(e.empty() ? "model load failed" : e);
         return nullptr;
     }
     return m;
+}
+
+fwb_model_t *fwb_model_open(const char *path, size_t max_ctx, int device) {
+    return open_model(path, max_ctx, device, 0, 1);
+}
+
+fwb_model_t *fwb_model_open_tp(const char *path, size_t max_ctx, int device, int rank, int world) {
+    return open_model(path, max_ctx, device, rank, world);
+}
+
+int fwb_tp_handle(fwb_model_t *m, void *handle) {
+    if (!m || !handle || m->world < 2) { set_err("fwb_tp_handle: not a tensor parallel model"); return -1; }
+    cudaSetDevice(m->dev);
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, m->xbuf) != cudaSuccess) { set_err("cudaIpcGetMemHandle failed"); return -1; }
+    static_assert(sizeof(h) == 64, "IPC handle size");
+    std::memcpy(handle, &h, sizeof(h));
+    return 0;
+}
+
+int fwb_tp_connect(fwb_model_t *m, const void *handles) {
+    if (!m || !handles || m->world < 2) { set_err("fwb_tp_connect: not a tensor parallel model"); return -1; }
+    if (m->connected) { set_err("fwb_tp_connect: already connected"); return -1; }
+    cudaSetDevice(m->dev);
+    const uint8_t *hb = static_cast<const uint8_t *>(handles);
+    for (uint32_t q = 0; q < m->world; ++q) {
+        if (q == m->rank) { m->peer[q] = m->xbuf; continue; }
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, hb + 64 * q, 64);
+        void *p = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            set_err(std::string("cudaIpcOpenMemHandle (rank ") + std::to_string(q) + "): " + cudaGetErrorString(e));
+            return -1;
+        }
+        m->peer[q] = static_cast<uint8_t *>(p);
+        m->peer_mapped[q] = true;
+    }
+    if (!build_steps(m) || (m->use_graph && !capture_graph(m))) return -1;
+    m->connected = true;
+    return 0;
+}
+
+int fwb_tp_shard(const char *path, const char *tensor, int as_head, int rank, int world, void *out, size_t cap,
+                 size_t *out_bytes) {
+    if (!path || !tensor || world < 1 || world > (int)kMaxRanks || rank < 0 || rank >= world) {
+        set_err("fwb_tp_shard: bad arguments");
+        return -1;
+    }
+    GgufFile f;
+    ModelConfig c;
+    std::string err;
+    if (!f.open(path, err) || !f.config(c, err) || !tp_check(c, (uint32_t)world, err)) { set_err(err); return -1; }
+    const GgufTensor *t = f.find(tensor);
+    if (!t) { set_err(std::string("fwb_tp_shard: no tensor ") + tensor); return -1; }
+    const uint32_t cols = (uint32_t)t->dims[0], rows = t->n_dims >= 2 ? (uint32_t)t->dims[1] : 1u;
+    const ShardSpec sp = tp_shard_spec(c, t->name, rows, cols, (uint32_t)rank, (uint32_t)world, as_head != 0);
+    const uint64_t n = tp_shard_bytes(*t, sp);
+    if (out_bytes) *out_bytes = n;
+    if (!out) return 0;
+    if (cap < n) { set_err("fwb_tp_shard: buffer too small"); return -1; }
+    tp_extract(*t, sp, static_cast<uint8_t *>(out));
+    return 0;
 }
 
 void fwb_model_close(fwb_model_t *m) {
@@ -1051,6 +1277,18 @@ int fwb_forward(fwb_model_t *m, uint32_t token, size_t pos, float *logits_host) 
     cudaSetDevice(m->dev);
     if (!set_step(m, token, pos) || !enqueue_step(m)) return -1;
     float *dst = logits_host ? logits_host : nullptr;
+    if (dst && m->world > 1) {
+        // every rank's slice: this rank's own and the peers' (mapped), after the
+        // step; the step's closing cross-rank barrier has seen every head phase
+        if (!finish(m)) return -1;
+        const size_t vr = m->cfg.n_vocab / m->world;
+        for (uint32_t q = 0; q < m->world; ++q)
+            if (cudaMemcpy(dst + q * vr, m->peer[q] + m->x_logits, vr * 4, cudaMemcpyDeviceToHost) != cudaSuccess) {
+                set_err("logits gather failed");
+                return -1;
+            }
+        return 0;
+    }
     if (dst) {
         cudaPointerAttributes pa;
         const bool pinned = cudaPointerGetAttributes(&pa, dst) == cudaSuccess && pa.type == cudaMemoryTypeHost;
@@ -1096,18 +1334,20 @@ static int kv_copy(fwb_model_t *m, size_t layer, size_t pos0, size_t n, float *k
     const ModelConfig &c = m->cfg;
     if (layer >= c.n_layer || pos0 > m->kv_ctx || n > m->kv_ctx - pos0) { set_err("kv: range"); return -1; }
     if (n == 0) return 0;
-    const size_t hd = c.head_dim, KV = c.n_head_kv;
-    const size_t base = layer * KV * m->kv_ctx * hd;
-    for (size_t h = 0; h < KV; ++h) {
+    // the host arrays hold every KV head; this rank's cache holds KV/world of them
+    const size_t hd = c.head_dim, KV = c.n_head_kv, KVr = KV / m->world, h0 = (size_t)m->rank * KVr;
+    const size_t base = layer * KVr * m->kv_ctx * hd;
+    for (size_t h = 0; h < KVr; ++h) {
         float *dk = m->kc + base + (h * m->kv_ctx + pos0) * hd;
         float *dv = m->vc + base + (h * m->kv_ctx + pos0) * hd;
+        const size_t hh = h0 + h;
         cudaError_t e1, e2;
         if (load) {
-            e1 = cudaMemcpy2DAsync(dk, hd * 4, k + h * hd, KV * hd * 4, hd * 4, n, cudaMemcpyHostToDevice, m->st);
-            e2 = cudaMemcpy2DAsync(dv, hd * 4, v + h * hd, KV * hd * 4, hd * 4, n, cudaMemcpyHostToDevice, m->st);
+            e1 = cudaMemcpy2DAsync(dk, hd * 4, k + hh * hd, KV * hd * 4, hd * 4, n, cudaMemcpyHostToDevice, m->st);
+            e2 = cudaMemcpy2DAsync(dv, hd * 4, v + hh * hd, KV * hd * 4, hd * 4, n, cudaMemcpyHostToDevice, m->st);
         } else {
-            e1 = cudaMemcpy2DAsync(k + h * hd, KV * hd * 4, dk, hd * 4, hd * 4, n, cudaMemcpyDeviceToHost, m->st);
-            e2 = cudaMemcpy2DAsync(v + h * hd, KV * hd * 4, dv, hd * 4, hd * 4, n, cudaMemcpyDeviceToHost, m->st);
+            e1 = cudaMemcpy2DAsync(k + hh * hd, KV * hd * 4, dk, hd * 4, hd * 4, n, cudaMemcpyDeviceToHost, m->st);
+            e2 = cudaMemcpy2DAsync(v + hh * hd, KV * hd * 4, dv, hd * 4, hd * 4, n, cudaMemcpyDeviceToHost, m->st);
         }
         if (e1 != cudaSuccess || e2 != cudaSuccess) { set_err("kv copy failed"); return -1; }
     }
@@ -1146,6 +1386,15 @@ int fwb_trace_read(fwb_model_t *m, uint64_t *out, size_t n, char *names, size_t 
             snprintf(names + i * name_stride, name_stride, "%s", m->steps[i].name.c_str());
     return (int)np;
 }
+int fwb_trace_cta_read(fwb_model_t *m, uint64_t *out, size_t n) {
+    if (!m || !m->persistent || !m->dargs.trace_cta) { set_err("tracing is off (set FWB_TRACE=1 before opening)"); return -1; }
+    const size_t cnt = (size_t)m->dargs.n_ph * m->sms;
+    if (n < cnt) { set_err("trace buffer too small"); return -1; }
+    cudaSetDevice(m->dev);
+    if (cudaMemcpy(out, m->dargs.trace_cta, cnt * 8, cudaMemcpyDeviceToHost) != cudaSuccess) { set_err("trace copy"); return -1; }
+    return (int)cnt;
+}
+
 void *fwb_stream(fwb_model_t *m) { return m ? (void *)m->st : nullptr; }
 
 }  // extern "C"

@@ -23,11 +23,33 @@ def _err(lib) -> str:
 class Model:
     """One decode model on one GPU (transformer_t of forword.c)."""
 
-    def __init__(self, path: str, max_ctx: int = 0, device: int = 0):
+    def __init__(self, path: str, max_ctx: int = 0, device: int = 0, rank: int = 0, world: int = 1,
+                 exchange=None):
+        """world > 1: rank `rank` of a tensor-parallel model (one process per
+        GPU).  `exchange(handle: bytes) -> list[bytes]` must all-gather the
+        64-byte exchange-buffer handles of every rank in rank order (e.g. with
+        torch.distributed.all_gather_object); see fwb.tp."""
         self.lib = native.product()
-        self.h = self.lib.fwb_model_open(path.encode(), max_ctx, device)
+        self.h = None
+        self.rank, self.world = rank, world
+        if world == 1:
+            self.h = self.lib.fwb_model_open(path.encode(), max_ctx, device)
+        else:
+            self.h = self.lib.fwb_model_open_tp(path.encode(), max_ctx, device, rank, world)
         if not self.h:
             raise FwbError(f"fwb_model_open({path}): {_err(self.lib)}")
+        if world > 1:
+            if exchange is None:
+                raise FwbError("a tensor-parallel model needs an exchange function")
+            mine = ctypes.create_string_buffer(64)
+            if self.lib.fwb_tp_handle(self.h, mine) != 0:
+                raise FwbError(f"fwb_tp_handle: {_err(self.lib)}")
+            handles = exchange(mine.raw)
+            if len(handles) != world or any(len(x) != 64 for x in handles):
+                raise FwbError("exchange must return one 64-byte handle per rank")
+            buf = ctypes.create_string_buffer(b"".join(handles), 64 * world)
+            if self.lib.fwb_tp_connect(self.h, buf) != 0:
+                raise FwbError(f"fwb_tp_connect: {_err(self.lib)}")
         d = (ctypes.c_uint32 * 8)()
         self.lib.fwb_model_dims(self.h, d)
         (self.n_vocab, self.kv_ctx, self.n_embd, self.n_layer, self.n_head, self.n_head_kv,
@@ -105,6 +127,19 @@ class Model:
         if self.lib.fwb_kv_read(self.h, layer, pos0, n, k.ctypes.data_as(fp), v.ctypes.data_as(fp)) != 0:
             raise FwbError(f"fwb_kv_read: {_err(self.lib)}")
         return k, v
+
+
+def tp_shard(path: str, tensor: str, rank: int, world: int, as_head: bool = False) -> np.ndarray:
+    """Host-only: the bytes rank `rank` of `world` keeps of `tensor` (fwb_tp_shard)."""
+    lib = native.product()
+    n = ctypes.c_size_t()
+    args = (path.encode(), tensor.encode(), int(as_head), rank, world)
+    if lib.fwb_tp_shard(*args, None, 0, ctypes.byref(n)) != 0:
+        raise FwbError(f"fwb_tp_shard: {_err(lib)}")
+    out = np.empty(n.value, dtype=np.uint8)
+    if lib.fwb_tp_shard(*args, out.ctypes.data, out.nbytes, ctypes.byref(n)) != 0:
+        raise FwbError(f"fwb_tp_shard: {_err(lib)}")
+    return out
 
 
 def quant_matvec(w: np.ndarray, ggml_type: int, x: np.ndarray, n_out: int) -> np.ndarray:

@@ -79,5 +79,10 @@ def _declare(lib) -> None:
     sig("fwb_stream", _vp, _vp)
     sig("fwb_trace_read", _i32, _vp, _c.POINTER(_u64), _sz, _c.c_char_p, _sz)
     sig("fwb_prof_read", _i32, _vp, _c.POINTER(_u64), _sz)
+    sig("fwb_trace_cta_read", _i32, _vp, _c.POINTER(_u64), _sz)
     sig("fwb_model_weight_bytes", _u64, _vp)
     sig("fwb_model_kernels_per_step", _i32, _vp)
+    sig("fwb_model_open_tp", _vp, _c.c_char_p, _sz, _i32, _i32, _i32)
+    sig("fwb_tp_handle", _i32, _vp, _vp)
+    sig("fwb_tp_connect", _i32, _vp, _vp)
+    sig("fwb_tp_shard", _i32, _c.c_char_p, _c.c_char_p, _i32, _i32, _i32, _vp, _sz, _c.POINTER(_sz))

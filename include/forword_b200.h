@@ -175,12 +175,61 @@ int fwb_kv_read(fwb_model_t *m, size_t layer, size_t pos0, size_t n, float *k, f
 int fwb_trace_read(fwb_model_t *m, uint64_t *out, size_t n, char *names, size_t name_stride);
 
 /*
+ * Barrier arrival time (GPU global timer, ns) of every CTA after every phase
+ * of the last step (FWB_TRACE=1): out[phase * n_sm + cta].  Shows which CTAs
+ * a barrier waits for.  Returns n_phases * n_sm, or -1.
+ */
+int fwb_trace_cta_read(fwb_model_t *m, uint64_t *out, size_t n);
+
+/*
  * Accumulated GEMV profile of the persistent kernel since the last read
  * (FWB_TRACE=1): out[(phase * n_sm + cta) * 4 + i] = ns that CTA spent in
  * i = 0 input prologue, 1 waiting for weight stages, 2 row loop, 3 tail.
  * Resets the counters.  Returns the number of values written, or -1.
  */
 int fwb_prof_read(fwb_model_t *m, uint64_t *out, size_t n);
+
+/* ------------------------------------------------------------------------
+ * Tensor parallelism across the GPUs of one box (no reference counterpart:
+ * forword.c runs on one CPU).  One process and one model handle per GPU;
+ * rank r of `world` (1..8) keeps its query/KV heads, its slice of the FFN and
+ * of the vocabulary, and the matching input columns of attn_output and
+ * ffn_down.  After o-proj and after down-proj the ranks' partial sums are
+ * added together inside the persistent decode kernel, each rank reading the
+ * others' partials over NVLink from their exchange buffers; every rank ends
+ * the step with the same residual stream and the same greedy token.
+ * ------------------------------------------------------------------------ */
+
+/*
+ * Open rank `rank` of a `world`-rank model on CUDA device `device`: uploads
+ * only this rank's slices.  n_head, n_head_kv and n_vocab must divide by
+ * world, and n_ff / world and (n_head / world) * head_dim must be multiples of
+ * 32.  The model can decode only after fwb_tp_connect.
+ */
+fwb_model_t *fwb_model_open_tp(const char *gguf_path, size_t max_ctx, int device, int rank, int world);
+
+/* 64-byte CUDA IPC handle of this rank's exchange buffer (send it to every rank). */
+int fwb_tp_handle(fwb_model_t *m, void *handle64);
+
+/*
+ * Map every rank's exchange buffer: handles = world consecutive 64-byte
+ * handles in rank order (this rank's own entry is ignored).  Builds the step.
+ * Every rank must then call the same forward functions with the same tokens
+ * and positions; a rank that stops leaves the others waiting until their
+ * bounded waits expire (an error, not a hang).  fwb_forward on any rank
+ * returns all n_vocab logits (the other ranks' slices are read over NVLink);
+ * fwb_logits_dev returns this rank's slice only.
+ */
+int fwb_tp_connect(fwb_model_t *m, const void *handles);
+
+/*
+ * Host only (no GPU): the bytes rank `rank` of `world` keeps of tensor
+ * `tensor` of a GGUF file, packed row-major in GGUF block layout.  as_head:
+ * the tensor is used as the LM head (vocabulary-row split).  With out NULL
+ * only *out_bytes is set.
+ */
+int fwb_tp_shard(const char *gguf_path, const char *tensor, int as_head, int rank, int world,
+                 void *out, size_t cap, size_t *out_bytes);
 
 /* Device logits of the last step (n_vocab fp32) and the model's CUDA stream. */
 const float *fwb_logits_dev(fwb_model_t *m);
