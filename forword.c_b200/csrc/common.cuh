@@ -67,9 +67,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 
 // Bounded wait for `parity` of an mbarrier phase.  Returns false (and sets
 // `code` in *err) when the bound is exceeded or another thread already
-// flagged an error.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t *err,
-                                          uint32_t code) {
+// flagged an error.  The first poll is inline (the phase has normally
+// completed already); the polling loop is out of line.
+__device__ __noinline__ bool mbar_wait_slow(uint64_t *bar, uint32_t parity, uint32_t *err, uint32_t code) {
     for (uint32_t i = 0; i < kMaxPolls; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
         if (i > 64) __nanosleep(i < 4096 ? 32 : 256);
@@ -77,6 +77,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32
     }
     atomicOr(err, code);
     return false;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t *err,
+                                          uint32_t code) {
+    if (mbar_try_wait(bar, parity)) return true;
+    return mbar_wait_slow(bar, parity, err, code);
 }
 
 // 1-D bulk copy global -> this CTA's shared memory, completing `bytes` of
