@@ -1,4 +1,5 @@
-"""Tensor-parallel decode on 2 GPUs (skipped with fewer): every rank runs
+"""Tensor-parallel decode on 2, 4 and 8 GPUs (each case skipped with fewer
+GPUs): every rank runs
 its slice of the model in its own process, the partial sums after o-proj and
 down-proj are added over NVLink inside the persistent kernel, and rank 0's
 logits (its own slice plus the peers', gathered by the library) must match
@@ -21,20 +22,16 @@ pytestmark = pytest.mark.gpu
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
-@pytest.fixture(scope="module")
-def two_gpus(built):
-    if native.product().fwb_device_count() < 2:
-        pytest.skip("needs 2 GPUs")
-    return True
-
-
-@pytest.mark.parametrize("cfg,seed", [(configs.SMALL_Q4_0, 41), (configs.SMALL_MIXED, 42)])
-def test_tp2_matches_oracle(two_gpus, tmp_path, cfg, seed):
+@pytest.mark.parametrize("cfg,seed,world", [(configs.SMALL_Q4_0, 41, 2), (configs.SMALL_MIXED, 42, 2),
+                                            (configs.SMALL_TP8, 43, 4), (configs.SMALL_TP8, 44, 8)])
+def test_tp_matches_oracle(built, tmp_path, cfg, seed, world):
+    if native.product().fwb_device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     path = gguf_synth.write_model(str(tmp_path / "tp.gguf"), cfg, seed=seed)
     out = str(tmp_path / "tp.npz")
     steps = 12
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
-    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={world}",
                         "--master-addr=127.0.0.1", "--master-port=29533", os.path.join(HERE, "tp_worker.py"),
                         path, out, str(steps)], env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]

@@ -2,8 +2,8 @@
 
 * The slice every rank keeps of every tensor (fwb_tp_shard, the rule the
   model upload uses) reassembles the whole tensor: row splits concatenate,
-  column splits (attn_output, ffn_down) join row by row.  Checked with two
-  gloo ranks in separate processes, each extracting its own slices.
+  column splits (attn_output, ffn_down) join row by row.  Checked with 2 and
+  4 gloo ranks in separate processes, each extracting its own slices.
 * The all-reduce identity behind the split: the ranks' partial products of
   attn_output / ffn_down (their input-column slices times their slices of
   the input) sum to the whole product, with the oracle's quant_matvec.
@@ -37,9 +37,9 @@ def model(built, tmp_path_factory):
     return gguf_synth.write_model(str(d / "tp.gguf"), CFG, seed=31)
 
 
-def _tensors():
+def _tensors(cfg=CFG):
     names = [("token_embd.weight", False), ("output.weight", True), ("output_norm.weight", False)]
-    for l in range(CFG.n_layer):
+    for l in range(cfg.n_layer):
         for t in ("attn_norm", "attn_q", "attn_k", "attn_v", "attn_output", "ffn_norm", "ffn_gate",
                   "ffn_up", "ffn_down"):
             names.append((f"blk.{l}.{t}.weight", False))
@@ -50,27 +50,22 @@ def _col_split(name: str) -> bool:
     return name.endswith("attn_output.weight") or name.endswith("ffn_down.weight")
 
 
-def _rows(name: str) -> int:
-    if name.endswith("attn_output.weight") or name.endswith("ffn_down.weight"):
-        return CFG.n_embd
-    return 0
-
-
-def _shard_worker(rank, world, port, path, errq):
+def _shard_worker(rank, world, port, path, cfg_name, errq):
     try:
+        cfg = configs.CONFIGS[cfg_name]
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
         dist.init_process_group("gloo", rank=rank, world_size=world)
-        mine = {n: tp_shard(path, n, rank, world, as_head=h).tobytes() for n, h in _tensors()}
+        mine = {n: tp_shard(path, n, rank, world, as_head=h).tobytes() for n, h in _tensors(cfg)}
         allp = [None] * world
         dist.all_gather_object(allp, mine)
         handles = gather_handles(bytes([rank]) * 64)
         assert handles == [bytes([q]) * 64 for q in range(world)]
         if rank == 0:
-            for n, h in _tensors():
+            for n, h in _tensors(cfg):
                 full = tp_shard(path, n, 0, 1, as_head=h)
                 parts = [np.frombuffer(p[n], dtype=np.uint8) for p in allp]
                 if _col_split(n):
-                    rows = _rows(n)
+                    rows = cfg.n_embd
                     got = np.concatenate([p.reshape(rows, -1) for p in parts], axis=1).reshape(-1)
                 elif n.endswith("norm.weight") or n == "token_embd.weight":
                     assert all(np.array_equal(p, full) for p in parts), n  # whole on every rank
@@ -85,11 +80,14 @@ def _shard_worker(rank, world, port, path, errq):
         raise
 
 
-def test_two_ranks_reassemble_every_tensor(model):
+@pytest.mark.parametrize("world", [2, 4])
+def test_ranks_reassemble_every_tensor(built, tmp_path, world):
+    cfg = CFG if world == 2 else configs.SMALL_TP8
+    model = gguf_synth.write_model(str(tmp_path / f"tp{world}.gguf"), cfg, seed=30 + world)
     ctx = mp.get_context("spawn")
     errq = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_shard_worker, args=(r, 2, port, model, errq)) for r in range(2)]
+    ps = [ctx.Process(target=_shard_worker, args=(r, world, port, model, cfg.name, errq)) for r in range(world)]
     for p in ps:
         p.start()
     for p in ps:
