@@ -29,7 +29,16 @@ struct AttnArgs {
     float scale;           // 1/sqrtf(head_dim), attention.c:143
     const uint32_t *step;  // [1] = pos
     uint32_t *err;
+    unsigned long long *trace;  // optional (tracing): every CTA's timeline of its item, [cta][8]
 };
+
+__device__ __forceinline__ void attn_stamp(const AttnArgs &a, int i) {
+    if (a.trace && threadIdx.x == 0) {
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+        a.trace[blockIdx.x * 8 + i] = t;
+    }
+}
 
 constexpr int kAttnWarps = 4;          // warps per CTA of the standalone kernel
 constexpr uint32_t kMinSplitPos = 64;   // positions per split at least
@@ -47,10 +56,76 @@ struct AttnSmem {
     float wm[NW][GQ], wl[NW][GQ];
     float wo[NW][GQ][HD];
     float wf[NW][GQ], wM[GQ];  // per-warp rescale factors exp(m_w - M) and the CTA maximum
-    float sw[kMaxSplits][GQ], sl[kMaxSplits][GQ];
-    float sL[GQ];
     uint32_t last_flag;
 };
+
+// Merge the n_use split partials of KV head h into the output (the last CTA
+// of the head to finish runs this).  One pass, one round of L2 loads for up
+// to 32 splits: a warp covers 32 consecutive output elements (query heads g0
+// and at most g0 + 1); lane s loads the (max, sum) pairs of split s (and
+// s + 32) for both heads, the warp reduces them to the head maximum M and the
+// weights f_s = exp(m_s - M), and every lane sums its element's split values
+// in split order with f_s taken from lane s by shuffle.
+template <int HD, int GQ>
+__device__ __noinline__ void attn_merge(const AttnArgs &a, uint32_t h, uint32_t n_use) {
+    constexpr uint32_t NE = (uint32_t)(GQ * HD), ST = HD + 2;
+    const uint32_t lane = threadIdx.x & 31;
+    const unsigned FULL = 0xffffffffu;
+    const float *P = a.part + (size_t)h * a.n_split * GQ * ST;
+    for (uint32_t i0 = (threadIdx.x & ~31u); i0 < NE; i0 += blockDim.x) {
+        const uint32_t i = min(i0 + lane, NE - 1);
+        const uint32_t g = i / HD, d = i % HD;
+        const uint32_t g0 = i0 / HD, g1 = min(g0 + 1, (uint32_t)GQ - 1);
+        // (max, sum) of splits lane and lane + 32 for heads g0 and g1
+        float mm[2][2], ll[2][2];
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                const uint32_t s = lane + 32u * k, gg = r ? g1 : g0;
+                const bool in = s < n_use;
+                mm[r][k] = in ? __ldcg(P + ((size_t)s * GQ + gg) * ST) : -INFINITY;
+                ll[r][k] = in ? __ldcg(P + ((size_t)s * GQ + gg) * ST + 1) : 0.f;
+            }
+        float v[32];
+#pragma unroll
+        for (uint32_t k = 0; k < 32; ++k)
+            v[k] = k < n_use ? __ldcg(P + ((size_t)k * GQ + g) * ST + 2 + d) : 0.f;
+        float M[2], L[2], f[2][2];
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            M[r] = fmaxf(mm[r][0], mm[r][1]);
+#pragma unroll
+            for (int o = 16; o; o >>= 1) M[r] = fmaxf(M[r], __shfl_xor_sync(FULL, M[r], o));
+#pragma unroll
+            for (int k = 0; k < 2; ++k) f[r][k] = mm[r][k] == -INFINITY ? 0.f : expf(mm[r][k] - M[r]);
+            L[r] = fmaf(ll[r][1], f[r][1], ll[r][0] * f[r][0]);
+#pragma unroll
+            for (int o = 16; o; o >>= 1) L[r] += __shfl_xor_sync(FULL, L[r], o);
+        }
+        const bool hi = g != g0;
+        float O = 0.f;
+#pragma unroll
+        for (uint32_t k = 0; k < 32; ++k) {
+            const float w0 = __shfl_sync(FULL, f[0][0], k), w1 = __shfl_sync(FULL, f[1][0], k);
+            if (k < n_use) O = fmaf(v[k], hi ? w1 : w0, O);
+        }
+        for (uint32_t s0 = 32; s0 < n_use; s0 += 16) {  // beyond 32 splits: 16 more per round trip
+            float u[16];
+#pragma unroll
+            for (uint32_t k = 0; k < 16; ++k)
+                u[k] = s0 + k < n_use ? __ldcg(P + ((size_t)(s0 + k) * GQ + g) * ST + 2 + d) : 0.f;
+#pragma unroll
+            for (uint32_t k = 0; k < 16; ++k) {
+                const uint32_t src = (s0 + k) & 31;
+                const float w0 = __shfl_sync(FULL, f[0][1], src), w1 = __shfl_sync(FULL, f[1][1], src);
+                if (s0 + k < n_use) O = fmaf(u[k], hi ? w1 : w0, O);
+            }
+        }
+        if (i0 + lane < NE) a.out[(size_t)(h * GQ + g) * HD + d] = __fdiv_rn(O, hi ? L[1] : L[0]);
+    }
+    if (threadIdx.x == 0) a.ticket[h] = 0;
+}
 
 // One work item: KV head h, split sp of n_use.  All NW warps of the CTA take
 // part.  K/V, q and the partials are read with L2-only loads (other CTAs of
@@ -88,6 +163,7 @@ __device__ void attn_item(const AttnArgs &a, uint32_t h, uint32_t sp, uint32_t n
     const float *kb = a.kc + (size_t)h * a.kv_ctx * HD + 4 * lane;
     const float *vb = a.vc + (size_t)h * a.kv_ctx * HD + 4 * lane;
 
+    attn_stamp(a, 0);
     for (uint32_t t0 = w0; t0 < w1; t0 += TILE) {
         float4 kt[TILE], vt[TILE];
 #pragma unroll
@@ -161,6 +237,7 @@ __device__ void attn_item(const AttnArgs &a, uint32_t h, uint32_t sp, uint32_t n
         __syncwarp();
     }
 
+    attn_stamp(a, 1);  // warp 0's positions done
     // merge the warps of this CTA
 #pragma unroll
     for (int g = 0; g < GQ; ++g) {
@@ -203,53 +280,22 @@ __device__ void attn_item(const AttnArgs &a, uint32_t h, uint32_t sp, uint32_t n
         pp[g * (HD + 2) + 2 + d] = O;
         if (d == 0) { pp[g * (HD + 2)] = sh.wM[g]; pp[g * (HD + 2) + 1] = L; }
     }
-    __threadfence();
+    attn_stamp(a, 2);  // partial written
+    // The CTA barrier orders every thread's partial before thread 0's release
+    // fence (cumulativity); the fence after the ticket makes the other CTAs'
+    // partials visible to this CTA's loads after the next barrier.
     __syncthreads();
-    if (tid == 0) sh.last_flag = (atomicAdd(&a.ticket[h], 1u) == n_use - 1) ? 1u : 0u;
-    __syncthreads();
-    if (sh.last_flag) {
-        __threadfence();
-        // merge the n_use partials of this KV head: first the per-split weights
-        // exp(m_s - M) (one load per (split, head)), then every output element
-        // sums its split values with independent L2 loads
-        const float *P = a.part + (size_t)h * a.n_split * GQ * (HD + 2);
-        // every (m, l) pair with one load each, all in flight; then shared
-        // memory only
-        for (uint32_t i = tid; i < n_use * GQ; i += blockDim.x) {
-            sh.sw[i / GQ][i % GQ] = __ldcg(P + (size_t)i * (HD + 2));
-            sh.sl[i / GQ][i % GQ] = __ldcg(P + (size_t)i * (HD + 2) + 1);
-        }
-        __syncthreads();
-        if (tid < (uint32_t)GQ) {
-            float M = -INFINITY;
-            for (uint32_t s = 0; s < n_use; ++s) M = fmaxf(M, sh.sw[s][tid]);
-            float L = 0.f;
-            for (uint32_t s = 0; s < n_use; ++s) {
-                const float f = sh.sw[s][tid] == -INFINITY ? 0.f : expf(sh.sw[s][tid] - M);
-                L = fmaf(sh.sl[s][tid], f, L);
-                sh.sw[s][tid] = f;
-            }
-            sh.sL[tid] = L;
-        }
-        __syncthreads();
-        // outputs: the split values of an element are loaded 16 at a time
-        // before they are summed (in split order)
-        for (uint32_t i = tid; i < (uint32_t)(GQ * HD); i += blockDim.x) {
-            const uint32_t g = i / HD, d = i % HD;
-            float O = 0.f;
-            for (uint32_t s0 = 0; s0 < n_use; s0 += 16) {
-                float v[16];
-#pragma unroll
-                for (uint32_t k = 0; k < 16; ++k)
-                    v[k] = s0 + k < n_use ? __ldcg(P + ((size_t)(s0 + k) * GQ + g) * (HD + 2) + 2 + d) : 0.f;
-#pragma unroll
-                for (uint32_t k = 0; k < 16; ++k)
-                    if (s0 + k < n_use) O = fmaf(v[k], sh.sw[s0 + k][g], O);
-            }
-            a.out[(size_t)(h * GQ + g) * HD + d] = __fdiv_rn(O, sh.sL[g]);
-        }
-        if (tid == 0) a.ticket[h] = 0;
+    attn_stamp(a, 3);
+    if (tid == 0) {
+        fence_acq_rel_gpu();
+        const bool last = atomicAdd(&a.ticket[h], 1u) == n_use - 1;
+        if (last) fence_acq_rel_gpu();
+        sh.last_flag = last ? 1u : 0u;
     }
+    __syncthreads();
+    attn_stamp(a, 4);  // ticket
+    if (sh.last_flag) attn_merge<HD, GQ>(a, h, n_use);
+    attn_stamp(a, 5);  // merged (last CTA) / done
     __syncthreads();  // the scratch may be reused by the next item
 }
 

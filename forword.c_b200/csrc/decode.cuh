@@ -78,6 +78,7 @@ struct DecodeArgs {
     uint32_t n_ph;
     uint32_t total_st;     // stages per CTA (max over CTAs is fine: CTAs read their own table)
     uint32_t NS, stage_bytes, scratch_bytes;
+    const uint32_t *step;  // [0] token, [1] position of this step
     uint32_t *sync;        // [0] barrier arrivals (zeroed before each launch), [1] abort
     uint32_t *err;
     uint32_t *n_st_cta;    // [gridDim.x] stages of each CTA
@@ -150,19 +151,21 @@ struct PhaseResult {
     bool ok;
 };
 
-// L2 prefetch of the K and V rows that this CTA's work items of the attention
-// phase `at` will read (the same item split as attn_phase_t).
-__device__ void prefetch_attn_kv(const AttnArgs &at, uint32_t hd, uint32_t pos) {
-    const uint32_t n_pos = pos + 1, n_use = attn_splits_in_use(at, n_pos);
-    const uint32_t chunk = (n_pos + n_use - 1) / n_use;
-    for (uint32_t it = blockIdx.x; it < at.n_kv * n_use; it += gridDim.x) {
-        const uint32_t h = it / n_use, sp = it % n_use;
-        const uint32_t c0 = min(n_pos, sp * chunk), c1 = min(n_pos, c0 + chunk);
-        if (c1 <= c0) continue;
-        const size_t off = ((size_t)h * at.kv_ctx + c0) * hd;
-        const uint32_t bytes = (c1 - c0) * hd * 4u;
-        bulk_prefetch_l2(at.kc + off, bytes);
-        bulk_prefetch_l2(at.vc + off, bytes);
+// L2 prefetch of the K and V rows [0, pos) of the layer whose QKV phase `g`
+// is next: the rows the attention phase after it reads besides the new one.
+// Issued a phase ahead, so HBM serves them while the QKV phase runs.  The
+// rows of every KV head are split evenly over the CTAs.
+__device__ __noinline__ void prefetch_kv_rows(const GemvArgs &g, uint32_t pos) {
+    const uint32_t hd = g.head_dim, nkv = hd ? g.n_kv / hd : 0u;
+    if (!pos || !nkv || pos > g.kv_ctx) return;
+    const uint32_t parts = max(1u, gridDim.x / nkv);
+    for (uint32_t it = blockIdx.x; it < nkv * parts; it += gridDim.x) {
+        const uint32_t h = it / parts, pt = it % parts;
+        const uint32_t r0 = (uint32_t)((uint64_t)pos * pt / parts), r1 = (uint32_t)((uint64_t)pos * (pt + 1) / parts);
+        if (r1 <= r0) continue;
+        const size_t off = ((size_t)h * g.kv_ctx + r0) * hd;
+        bulk_prefetch_l2(g.kcache + off, (r1 - r0) * hd * 4u);
+        bulk_prefetch_l2(g.vcache + off, (r1 - r0) * hd * 4u);
     }
 }
 
@@ -170,20 +173,19 @@ __device__ void prefetch_attn_kv(const AttnArgs &at, uint32_t hd, uint32_t pos) 
 // when another CTA already gave up (the abort flag sync[1]), it sets the
 // abort flag and returns false.  While waiting, the CTAs start the next
 // phase `nx`'s first reads that miss L2: a GEMV's RMSNorm weight (128 bytes
-// per CTA) or the attention phase's K/V rows.
-__device__ bool grid_sync(uint32_t *sync, uint32_t epoch, uint32_t *err, const Phase *nx) {
+// per CTA) and, before a QKV phase, the K/V rows of the attention after it.
+// pos: the step's position.
+__device__ bool grid_sync(uint32_t *sync, uint32_t epoch, uint32_t *err, const Phase *nx, uint32_t pos) {
     __shared__ uint32_t ok_flag;
     __syncthreads();
     if (threadIdx.x == 0) {
-        const bool kv = nx && nx->kind == PH_ATTN;
-        const uint32_t pos = kv ? __ldcg(&nx->at.step[1]) : 0u;
         // release: this CTA's writes of the phase become visible with the add;
         // acquire: the other CTAs' writes are visible once the count is seen
         red_release_add(&sync[0], 1u);
         if (nx && nx->kind == PH_GEMV && nx->g.norm && blockIdx.x * 128u < nx->g.K * 4u)
             bulk_prefetch_l2(reinterpret_cast<const uint8_t *>(nx->g.norm_w) + blockIdx.x * 128u,
                              min(128u, nx->g.K * 4u - blockIdx.x * 128u));
-        if (kv && pos < nx->at.kv_ctx) prefetch_attn_kv(nx->at, nx->hd, pos);
+        if (nx && nx->kind == PH_GEMV && nx->mode == GM_QKV) prefetch_kv_rows(nx->g, pos);
         const uint32_t target = epoch * gridDim.x;
         uint32_t ok = 0;
         for (uint32_t i = 0; i < (1u << 25); ++i) {
@@ -277,18 +279,18 @@ __device__ void tp_argmax_phase(const TpArgmaxArgs &a) {
 }
 
 template <int HD, int GQ>
-__device__ __noinline__ void attn_phase_t(const AttnArgs &a, uint8_t *scratch) {
+__device__ __noinline__ void attn_phase_t(const AttnArgs &a, uint8_t *scratch, uint32_t pos) {
     auto &sh = *reinterpret_cast<AttnSmem<HD, GQ, kDecodeThreads / 32> *>(scratch);
-    const uint32_t n_pos = __ldcg(&a.step[1]) + 1;
+    const uint32_t n_pos = pos + 1;
     const uint32_t n_use = attn_splits_in_use(a, n_pos);
     const uint32_t n_kv = a.n_kv;
     for (uint32_t it = blockIdx.x; it < n_kv * n_use; it += gridDim.x)
         attn_item<HD, GQ, kDecodeThreads / 32>(a, it / n_use, it % n_use, n_pos, n_use, sh);
 }
 
-__device__ void attn_phase(const Phase &P, uint8_t *scratch) {
+__device__ void attn_phase(const Phase &P, uint8_t *scratch, uint32_t pos) {
 #define FWB_ATTN(HDv, GQv) \
-    if (P.hd == HDv && P.gq == GQv) { attn_phase_t<HDv, GQv>(P.at, scratch); return; }
+    if (P.hd == HDv && P.gq == GQv) { attn_phase_t<HDv, GQv>(P.at, scratch, pos); return; }
     FWB_ATTN(128, 4) FWB_ATTN(128, 8) FWB_ATTN(128, 2) FWB_ATTN(128, 1)
     FWB_ATTN(64, 1) FWB_ATTN(64, 2) FWB_ATTN(64, 4) FWB_ATTN(64, 8)
     FWB_ATTN(48, 1) FWB_ATTN(48, 2) FWB_ATTN(48, 4) FWB_ATTN(48, 8)
@@ -355,6 +357,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
     }
 
     RingState rs{0, 0, 0};
+    // the step's position (fixed during the launch: only the last phase of a
+    // greedy step advances it, for the next launch)
+    const uint32_t pos = __ldcg(&d.step[1]);
     // cross-rank barriers completed before this step, and during it
     const unsigned long long gbase = d.world > 1 ? __ldcg(d.gbase) : 0ull;
     uint32_t gk = 0;
@@ -392,7 +397,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
                 rs = r.rs;
                 ok = ok && r.ok;
             } else if (P.kind == PH_ATTN) {
-                attn_phase(P, smem + kHeaderBytes);
+                attn_phase(P, smem + kHeaderBytes, pos);
             } else if (P.kind == PH_ALLREDUCE) {
                 allreduce_phase(P.ar);
             } else if (P.kind == PH_TPARGMAX) {
@@ -431,7 +436,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
                 ++gk;
                 if (!global_sync(d, (gbase + gk) * (unsigned long long)d.world * gridDim.x)) ok = false;
                 if (tid == 0) red_release_add(&d.sync[0], 1u);
-            } else if (!grid_sync(d.sync, p + 1, d.err, &N)) {
+            } else if (!grid_sync(d.sync, p + 1, d.err, &N, pos)) {
                 ok = false;
             }
         }

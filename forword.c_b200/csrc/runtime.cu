@@ -405,6 +405,7 @@ struct fwb_model {
     bool peer_mapped[fwb::kMaxRanks] = {};
     unsigned long long *gbase = nullptr;
     bool connected = false;
+    unsigned long long *attn_trace = nullptr;  // FWB_TRACE: [layer][8] CTA 0's attention item timeline
 };
 
 namespace fwb {
@@ -769,6 +770,9 @@ static bool build_steps(fwb_model *m) {
         return true;
     };
 
+    const char *trc = getenv("FWB_TRACE");
+    if (trc && *trc == '1' && !m->attn_trace && !dalloc(m, (void **)&m->attn_trace, (size_t)c.n_layer * m->sms * 8 * 8))
+        return false;
     const uint32_t nsplit = attn_splits(m);
     if (!dalloc(m, (void **)&m->attn_part, (size_t)KVr * nsplit * (H / KV) * (hd + 2) * 4)) return false;
     const void *afn = attn_fn(hd, H / KV);
@@ -803,6 +807,7 @@ static bool build_steps(fwb_model *m) {
             a.n_split = nsplit;
             a.scale = 1.0f / sqrtf((float)hd);
             a.step = m->step;
+            if (m->attn_trace) a.trace = m->attn_trace + (size_t)l * m->sms * 8;
             a.err = m->err;
             s.bytes = 0;  // KV bytes depend on pos; accounted separately
             a.n_kv = KVr;
@@ -909,7 +914,7 @@ static bool build_decode(fwb_model *m) {
         const uint32_t nw = kDecodeThreads / 32;
         // the layout itself, and a formula check that every member is covered
         const uint32_t att = std::max<uint32_t>(attn_smem_bytes(hd, gq),
-                                                (nw * 32 + 3 * nw * gq + nw * gq * hd + 2 * kMaxSplits * gq + 2 * gq + 1) * 4);
+                                                (nw * 32 + 3 * nw * gq + nw * gq * hd + gq + 1) * 4);
         scratch = std::max(scratch, (att + 127) / 128 * 128);
     }
     cudaFuncAttributes fa;
@@ -973,6 +978,7 @@ static bool build_decode(fwb_model *m) {
     d.NS = ns;
     d.stage_bytes = stage;
     d.scratch_bytes = scratch;
+    d.step = m->step;
     d.sync = m->sync;
     d.err = m->err;
     d.n_st_cta = d_nst;
@@ -1392,6 +1398,16 @@ int fwb_trace_cta_read(fwb_model_t *m, uint64_t *out, size_t n) {
     if (n < cnt) { set_err("trace buffer too small"); return -1; }
     cudaSetDevice(m->dev);
     if (cudaMemcpy(out, m->dargs.trace_cta, cnt * 8, cudaMemcpyDeviceToHost) != cudaSuccess) { set_err("trace copy"); return -1; }
+    return (int)cnt;
+}
+
+int fwb_trace_attn_read(fwb_model_t *m, uint64_t *out, size_t n) {
+    if (!m || !m->attn_trace) { set_err("tracing is off (set FWB_TRACE=1 before opening)"); return -1; }
+    const size_t cnt = (size_t)m->cfg.n_layer * m->sms * 8;
+    if (n < cnt) { set_err("trace buffer too small"); return -1; }
+    cudaSetDevice(m->dev);
+    if (cudaMemcpy(out, m->attn_trace, cnt * 8, cudaMemcpyDeviceToHost) != cudaSuccess) { set_err("trace copy"); return -1; }
+    CK(cudaMemset(m->attn_trace, 0, cnt * 8));  // CTAs without an item in the next step stay 0
     return (int)cnt;
 }
 

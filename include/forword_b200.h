@@ -182,6 +182,15 @@ int fwb_trace_read(fwb_model_t *m, uint64_t *out, size_t n, char *names, size_t 
 int fwb_trace_cta_read(fwb_model_t *m, uint64_t *out, size_t n);
 
 /*
+ * Timeline of every CTA's attention work item in every layer of the last
+ * step (FWB_TRACE=1): out[(layer * n_sm + cta) * 8 + i], GPU global timer (ns)
+ * at i = 0 start, 1 its warp 0 done with its positions, 2 partial written,
+ * 3 CTA barrier passed, 4 split ticket taken, 5 item done; 0 for CTAs without
+ * an item.  Clears the record.  Returns n_layer * n_sm * 8, or -1.
+ */
+int fwb_trace_attn_read(fwb_model_t *m, uint64_t *out, size_t n);
+
+/*
  * Accumulated GEMV profile of the persistent kernel since the last read
  * (FWB_TRACE=1): out[(phase * n_sm + cta) * 4 + i] = ns that CTA spent in
  * i = 0 input prologue, 1 waiting for weight stages, 2 row loop, 3 tail.
