@@ -56,75 +56,76 @@ struct AttnSmem {
     float wm[NW][GQ], wl[NW][GQ];
     float wo[NW][GQ][HD];
     float wf[NW][GQ], wM[GQ];  // per-warp rescale factors exp(m_w - M) and the CTA maximum
+    float mw[GQ][kMaxSplits], mL[GQ];  // split merge: per-split weights and the total per head
     uint32_t last_flag;
 };
 
 // Merge the n_use split partials of KV head h into the output (the last CTA
-// of the head to finish runs this).  One pass, one round of L2 loads for up
-// to 32 splits: a warp covers 32 consecutive output elements (query heads g0
-// and at most g0 + 1); lane s loads the (max, sum) pairs of split s (and
-// s + 32) for both heads, the warp reduces them to the head maximum M and the
-// weights f_s = exp(m_s - M), and every lane sums its element's split values
-// in split order with f_s taken from lane s by shuffle.
-template <int HD, int GQ>
-__device__ __noinline__ void attn_merge(const AttnArgs &a, uint32_t h, uint32_t n_use) {
+// of the head to finish runs this; all its threads).  Warp g (one per query
+// head) loads the (max, sum) pairs of the splits, one split per lane, and
+// turns them into the weights f_s = exp(m_s - M) and the total L in shared
+// memory; meanwhile every thread has its element's split values in flight
+// (one coalesced load per split).  After one CTA barrier each thread sums its
+// values in split order with the weights read from shared memory.
+template <int HD, int GQ, int NW>
+__device__ __noinline__ void attn_merge(const AttnArgs &a, uint32_t h, uint32_t n_use, AttnSmem<HD, GQ, NW> &sh) {
     constexpr uint32_t NE = (uint32_t)(GQ * HD), ST = HD + 2;
-    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const unsigned FULL = 0xffffffffu;
     const float *P = a.part + (size_t)h * a.n_split * GQ * ST;
-    for (uint32_t i0 = (threadIdx.x & ~31u); i0 < NE; i0 += blockDim.x) {
-        const uint32_t i = min(i0 + lane, NE - 1);
-        const uint32_t g = i / HD, d = i % HD;
-        const uint32_t g0 = i0 / HD, g1 = min(g0 + 1, (uint32_t)GQ - 1);
-        // (max, sum) of splits lane and lane + 32 for heads g0 and g1
-        float mm[2][2], ll[2][2];
+    const long long c0 = clock64();
+    // this thread's element (the first of them when NE > blockDim.x)
+    const uint32_t i_first = min(tid, NE - 1), g_first = i_first / HD, d_first = i_first % HD;
+    const uint32_t n_a = min(n_use, 32u);
+    float v[32];
 #pragma unroll
-        for (int r = 0; r < 2; ++r)
+    for (uint32_t k = 0; k < 32; ++k)
+        v[k] = k < n_a ? __ldcg(P + ((size_t)k * GQ + g_first) * ST + 2 + d_first) : 0.f;
+    for (uint32_t g = warp; g < (uint32_t)GQ; g += blockDim.x >> 5) {
+        float2 ml[2];
 #pragma unroll
-            for (int k = 0; k < 2; ++k) {
-                const uint32_t s = lane + 32u * k, gg = r ? g1 : g0;
-                const bool in = s < n_use;
-                mm[r][k] = in ? __ldcg(P + ((size_t)s * GQ + gg) * ST) : -INFINITY;
-                ll[r][k] = in ? __ldcg(P + ((size_t)s * GQ + gg) * ST + 1) : 0.f;
-            }
-        float v[32];
-#pragma unroll
-        for (uint32_t k = 0; k < 32; ++k)
-            v[k] = k < n_use ? __ldcg(P + ((size_t)k * GQ + g) * ST + 2 + d) : 0.f;
-        float M[2], L[2], f[2][2];
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            M[r] = fmaxf(mm[r][0], mm[r][1]);
-#pragma unroll
-            for (int o = 16; o; o >>= 1) M[r] = fmaxf(M[r], __shfl_xor_sync(FULL, M[r], o));
-#pragma unroll
-            for (int k = 0; k < 2; ++k) f[r][k] = mm[r][k] == -INFINITY ? 0.f : expf(mm[r][k] - M[r]);
-            L[r] = fmaf(ll[r][1], f[r][1], ll[r][0] * f[r][0]);
-#pragma unroll
-            for (int o = 16; o; o >>= 1) L[r] += __shfl_xor_sync(FULL, L[r], o);
+        for (int k = 0; k < 2; ++k) {
+            const uint32_t s = lane + 32u * k;
+            ml[k] = s < n_use ? __ldcg(reinterpret_cast<const float2 *>(P + ((size_t)s * GQ + g) * ST))
+                              : make_float2(-INFINITY, 0.f);
         }
-        const bool hi = g != g0;
-        float O = 0.f;
+        float M = fmaxf(ml[0].x, ml[1].x);
 #pragma unroll
-        for (uint32_t k = 0; k < 32; ++k) {
-            const float w0 = __shfl_sync(FULL, f[0][0], k), w1 = __shfl_sync(FULL, f[1][0], k);
-            if (k < n_use) O = fmaf(v[k], hi ? w1 : w0, O);
+        for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(FULL, M, o));
+        float f[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) f[k] = ml[k].x == -INFINITY ? 0.f : expf(ml[k].x - M);
+        float L = fmaf(ml[1].y, f[1], ml[0].y * f[0]);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(FULL, L, o);
+        sh.mw[g][lane] = f[0];
+        sh.mw[g][lane + 32] = f[1];
+        if (lane == 0) sh.mL[g] = L;
+    }
+    __syncthreads();
+    if (a.trace && tid == 0) a.trace[blockIdx.x * 8 + 6] = clock64() - c0;  // weights ready (SM clocks)
+    for (uint32_t i = tid; i < NE; i += blockDim.x) {
+        const uint32_t g = i / HD, d = i % HD;
+        float O = 0.f;
+        if (i == tid) {
+#pragma unroll
+            for (uint32_t k = 0; k < 32; ++k)
+                if (k < n_a) O = fmaf(v[k], sh.mw[g][k], O);
+        } else {  // a further element of this thread (small CTAs)
+            for (uint32_t k = 0; k < n_a; ++k) O = fmaf(__ldcg(P + ((size_t)k * GQ + g) * ST + 2 + d), sh.mw[g][k], O);
         }
         for (uint32_t s0 = 32; s0 < n_use; s0 += 16) {  // beyond 32 splits: 16 more per round trip
             float u[16];
 #pragma unroll
-            for (uint32_t k = 0; k < 16; ++k)
-                u[k] = s0 + k < n_use ? __ldcg(P + ((size_t)(s0 + k) * GQ + g) * ST + 2 + d) : 0.f;
+            for (uint32_t k = 0; k < 16; ++k) u[k] = s0 + k < n_use ? __ldcg(P + ((size_t)(s0 + k) * GQ + g) * ST + 2 + d) : 0.f;
 #pragma unroll
-            for (uint32_t k = 0; k < 16; ++k) {
-                const uint32_t src = (s0 + k) & 31;
-                const float w0 = __shfl_sync(FULL, f[0][1], src), w1 = __shfl_sync(FULL, f[1][1], src);
-                if (s0 + k < n_use) O = fmaf(u[k], hi ? w1 : w0, O);
-            }
+            for (uint32_t k = 0; k < 16; ++k)
+                if (s0 + k < n_use) O = fmaf(u[k], sh.mw[g][s0 + k], O);
         }
-        if (i0 + lane < NE) a.out[(size_t)(h * GQ + g) * HD + d] = __fdiv_rn(O, hi ? L[1] : L[0]);
+        a.out[(size_t)(h * GQ + g) * HD + d] = __fdiv_rn(O, sh.mL[g]);
     }
-    if (threadIdx.x == 0) a.ticket[h] = 0;
+    if (a.trace && tid == 0) a.trace[blockIdx.x * 8 + 7] = clock64() - c0;
+    if (tid == 0) a.ticket[h] = 0;
 }
 
 // One work item: KV head h, split sp of n_use.  All NW warps of the CTA take
@@ -294,7 +295,7 @@ __device__ void attn_item(const AttnArgs &a, uint32_t h, uint32_t sp, uint32_t n
     }
     __syncthreads();
     attn_stamp(a, 4);  // ticket
-    if (sh.last_flag) attn_merge<HD, GQ>(a, h, n_use);
+    if (sh.last_flag) attn_merge<HD, GQ, NW>(a, h, n_use, sh);
     attn_stamp(a, 5);  // merged (last CTA) / done
     __syncthreads();  // the scratch may be reused by the next item
 }

@@ -306,7 +306,8 @@ __device__ void attn_phase(const Phase &P, uint8_t *scratch, uint32_t pos) {
 // (instruction-cache footprint).
 template <int QT, bool A4>
 __device__ __noinline__ PhaseResult gemv_phase_t(const GemvArgs *g, GemvSmem sm, RingState rs, const StageSrc *tab,
-                                                 uint32_t n_ph, uint32_t total, uint32_t NS, uint32_t stage_bytes) {
+                                                 uint32_t n_ph, uint32_t total, uint32_t NS, uint32_t stage_bytes,
+                                                 uint32_t pos) {
     uint8_t *ring = sm.ring;
     uint64_t *full = sm.full;
     uint32_t *cursor = sm.done + kMaxStages;  // phase cursor word, next to the counters
@@ -314,16 +315,16 @@ __device__ __noinline__ PhaseResult gemv_phase_t(const GemvArgs *g, GemvSmem sm,
         if (j + NS < total) issue_global(tab, n_ph, j + NS, ring, stage_bytes, full, slot, cursor);
     };
     PhaseResult r;
-    r.ok = gemv_consume<QT, A4>(*g, sm, threadIdx.x, rs, refill);
+    r.ok = gemv_consume<QT, A4>(*g, sm, threadIdx.x, rs, refill, pos);
     r.rs = rs;
     return r;
 }
 
 template <int QT>
 __device__ PhaseResult gemv_phase_q(const Phase &P, const GemvSmem &sm, const RingState &rs, const StageSrc *tab,
-                                    uint32_t n_ph, uint32_t total, uint32_t NS, uint32_t stage_bytes) {
-    return P.a4 ? gemv_phase_t<QT, true>(&P.g, sm, rs, tab, n_ph, total, NS, stage_bytes)
-                : gemv_phase_t<QT, false>(&P.g, sm, rs, tab, n_ph, total, NS, stage_bytes);
+                                    uint32_t n_ph, uint32_t total, uint32_t NS, uint32_t stage_bytes, uint32_t pos) {
+    return P.a4 ? gemv_phase_t<QT, true>(&P.g, sm, rs, tab, n_ph, total, NS, stage_bytes, pos)
+                : gemv_phase_t<QT, false>(&P.g, sm, rs, tab, n_ph, total, NS, stage_bytes, pos);
 }
 
 __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_constant__ DecodeArgs d) {
@@ -389,9 +390,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
                 sm.red = reinterpret_cast<float *>(smem + kHeaderBytes + plane_bytes(P.g.K));
                 PhaseResult r{rs, false};
                 switch (P.qt) {
-                case QT_Q4_0: r = gemv_phase_q<QT_Q4_0>(P, sm, rs, tab, d.n_ph, total, d.NS, d.stage_bytes); break;
-                case QT_Q5_0: r = gemv_phase_q<QT_Q5_0>(P, sm, rs, tab, d.n_ph, total, d.NS, d.stage_bytes); break;
-                case QT_Q8_0: r = gemv_phase_q<QT_Q8_0>(P, sm, rs, tab, d.n_ph, total, d.NS, d.stage_bytes); break;
+                case QT_Q4_0: r = gemv_phase_q<QT_Q4_0>(P, sm, rs, tab, d.n_ph, total, d.NS, d.stage_bytes, pos); break;
+                case QT_Q5_0: r = gemv_phase_q<QT_Q5_0>(P, sm, rs, tab, d.n_ph, total, d.NS, d.stage_bytes, pos); break;
+                case QT_Q8_0: r = gemv_phase_q<QT_Q8_0>(P, sm, rs, tab, d.n_ph, total, d.NS, d.stage_bytes, pos); break;
                 default: break;
                 }
                 rs = r.rs;

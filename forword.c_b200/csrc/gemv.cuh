@@ -69,6 +69,8 @@ constexpr int kMaxStages = 8;
 constexpr uint32_t kMaxConsumers = 512;  // threads per GEMV CTA (all consumers)
 constexpr uint32_t kHeaderBytes = 1024;  // barriers, stage counters, small scratch
 constexpr uint32_t kStageSlack = 128;  // alignment + half-unit over-read room
+constexpr uint32_t kPosUnknown = 0xffffffffu;  // gemv_consume reads the position from step[1]
+constexpr uint32_t kProfSlots = 8;  // GEMV profile values per CTA and phase
 constexpr int kXMax = 32767;        // fixed-point range of the inputs (16 bits per value)
 
 struct GemvArgs {
@@ -103,7 +105,9 @@ struct GemvArgs {
                            // maximum goes here instead of advancing the step
     uint32_t *err;
     // optional profile: thread 0 of each CTA adds ns spent in
-    // [0] prologue (norm + planes), [1] waiting for stages, [2] the row loop, [3] tail
+    // [0] prologue (norm + planes), [1] waiting for stages, [2] the row loop, [3] tail,
+    // and from the phase start to [4] its first input loads landing, [5] the input
+    // planes' barrier; [6] from its own loop end until every warp's (kProfSlots per CTA)
     unsigned long long *prof;
 };
 
@@ -392,7 +396,8 @@ __device__ __forceinline__ void ring_advance(RingState &rs, uint32_t NS) {
 // 1/sqrtf(sum(x^2)/K + eps) (IEEE division and square root; every thread
 // sums the warp partials in the same order), or 1 without the norm.
 template <int OFF>
-__device__ float build_planes(const GemvArgs &a, const GemvSmem &sm, uint32_t tid, uint32_t NC) {
+__device__ float build_planes(const GemvArgs &a, const GemvSmem &sm, uint32_t tid, uint32_t NC, bool prof,
+                              unsigned long long &t_x, unsigned long long &t_b) {
     constexpr int kPass = 4;
     const bool norm = a.norm != 0;
     const uint32_t nb = a.K >> 5, nbp = sm.nbp;
@@ -437,6 +442,7 @@ __device__ float build_planes(const GemvArgs &a, const GemvSmem &sm, uint32_t ti
             }
             m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
             m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+            if (prof && b0 == 0 && p == 0) t_x = gtime_ns();  // the first loads have landed
             const bool bad = !isfinite(chk) || !isfinite(m);
             const float inv = m > 1e-30f && !bad ? (float)kXMax / m : 0.f;
             int xi[8], sum = 0;
@@ -472,6 +478,7 @@ __device__ float build_planes(const GemvArgs &a, const GemvSmem &sm, uint32_t ti
         if (lane == 0) sm.misc[warp] = ss;
     }
     bar_sync(1, NC);
+    if (prof) t_b = gtime_ns();
     if (!norm) return 1.0f;
     float t = 0.f;
     for (uint32_t w = 0; w < (NC >> 5); ++w) t += sm.misc[w];
@@ -511,7 +518,7 @@ __device__ __forceinline__ void rope_pair(float v0, float v1, float c, float s, 
 // barrier, then the epilogue over all local rows.
 template <int QT, bool A4, class Refill>
 __device__ bool gemv_consume(const GemvArgs &a, const GemvSmem &sm, uint32_t tid, RingState &rs,
-                             const Refill &refill) {
+                             const Refill &refill, uint32_t pos_known = kPosUnknown) {
     // run-time: the mode only changes the prologue / epilogue, pairing only the
     // per-thread row offsets (one copy of the row loop per quant type)
     const uint32_t MODE = a.mode;
@@ -542,9 +549,10 @@ __device__ bool gemv_consume(const GemvArgs &a, const GemvSmem &sm, uint32_t tid
     float pre_y = 0.f;
     uint32_t pos = 0;
     if (MODE == GM_RESID && tid < n_loc) pre_y = __ldcg(&a.y[rb + tid]);
-    if (MODE == GM_QKV) pos = __ldcg(&a.step[1]);
+    if (MODE == GM_QKV) pos = pos_known != kPosUnknown ? pos_known : __ldcg(&a.step[1]);
 
-    const float rscale = build_planes<OFF>(a, sm, tid, NC);
+    unsigned long long t_x = 0ull, t_b = 0ull;
+    const float rscale = build_planes<OFF>(a, sm, tid, NC, prof, t_x, t_b);
     XBlock xa, xb;
     load_planes(sm, unit_c, rscale, xa, xb);
 
@@ -559,6 +567,10 @@ __device__ bool gemv_consume(const GemvArgs &a, const GemvSmem &sm, uint32_t tid
         }
     }
     const unsigned long long t1 = prof ? gtime_ns() : 0ull;
+    if (prof) {  // (folded in now: no timer stays live through the row loop; no-return adds)
+        atomicAdd(&a.prof[(size_t)blockIdx.x * kProfSlots + 4], t_x - t0);
+        atomicAdd(&a.prof[(size_t)blockIdx.x * kProfSlots + 5], t_b - t0);
+    }
 
     // One ring stage per round: local stage k holds local rows [k*RS, (k+1)*RS).
     const uint32_t n_rounds = (n_loc + RS - 1) / RS;
@@ -636,6 +648,7 @@ __device__ bool gemv_consume(const GemvArgs &a, const GemvSmem &sm, uint32_t tid
 
     const unsigned long long t2 = prof ? gtime_ns() : 0ull;
     bar_sync(1, NC);  // every partial sum is parked
+    if (prof) atomicAdd(&a.prof[(size_t)blockIdx.x * kProfSlots + 6], gtime_ns() - t2);
 
     // ---- epilogue over all local rows
     float best_v = -INFINITY;
@@ -758,11 +771,11 @@ __device__ bool gemv_consume(const GemvArgs &a, const GemvSmem &sm, uint32_t tid
         bar_sync(1, NC);
     }
     if (prof) {
-        unsigned long long *pp = a.prof + (size_t)blockIdx.x * 4;
-        pp[0] += t1 - t0;
-        pp[1] += t_wait;
-        pp[2] += t2 - t1;
-        pp[3] += gtime_ns() - t2;
+        unsigned long long *pp = a.prof + (size_t)blockIdx.x * kProfSlots;
+        atomicAdd(&pp[0], t1 - t0);
+        atomicAdd(&pp[1], t_wait);
+        atomicAdd(&pp[2], t2 - t1);
+        atomicAdd(&pp[3], gtime_ns() - t2);
     }
     return ok;
 }

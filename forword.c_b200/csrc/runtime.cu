@@ -391,7 +391,7 @@ struct fwb_model {
     cudaGraphExec_t exec = nullptr;
     bool use_graph = true, use_pdl = true;
     bool persistent = true;          // one persistent kernel per token (else one kernel per phase)
-    unsigned long long *prof = nullptr;  // [n_phases][G][4] GEMV profile (FWB_TRACE=1)
+    unsigned long long *prof = nullptr;  // [n_phases][G][kProfSlots] GEMV profile (FWB_TRACE=1)
     fwb::DecodeArgs dargs{};
     size_t dsmem = 0;
     uint32_t *sync = nullptr;
@@ -914,7 +914,7 @@ static bool build_decode(fwb_model *m) {
         const uint32_t nw = kDecodeThreads / 32;
         // the layout itself, and a formula check that every member is covered
         const uint32_t att = std::max<uint32_t>(attn_smem_bytes(hd, gq),
-                                                (nw * 32 + 3 * nw * gq + nw * gq * hd + gq + 1) * 4);
+                                                (nw * 32 + 3 * nw * gq + nw * gq * hd + gq + gq * kMaxSplits + gq + 1) * 4);
         scratch = std::max(scratch, (att + 127) / 128 * 128);
     }
     cudaFuncAttributes fa;
@@ -926,13 +926,13 @@ static bool build_decode(fwb_model *m) {
     if (const char *e = getenv("FWB_MAX_NS")) ns = std::max(2u, std::min(ns, (uint32_t)atoi(e)));
     const char *trc = getenv("FWB_TRACE");
     const bool tracing = trc && *trc == '1';
-    if (tracing && !dalloc(m, (void **)&m->prof, (size_t)n_ph * G * 4 * 8)) return false;
+    if (tracing && !dalloc(m, (void **)&m->prof, (size_t)n_ph * G * kProfSlots * 8)) return false;
     for (uint32_t i = 0; i < n_ph; ++i) {
         Phase &p = ph[i];
         if (p.kind == PH_GEMV) {
             p.g.NS = ns;
             p.g.stage_bytes = stage;
-            p.g.prof = tracing ? m->prof + (size_t)i * G * 4 : nullptr;
+            p.g.prof = tracing ? m->prof + (size_t)i * G * kProfSlots : nullptr;
         }
     }
     // per-CTA stream tables
@@ -1373,7 +1373,7 @@ const float *fwb_logits_dev(fwb_model_t *m) { return m ? m->logits : nullptr; }
 
 int fwb_prof_read(fwb_model_t *m, uint64_t *out, size_t n) {
     if (!m || !m->prof) { set_err("profiling is off (set FWB_TRACE=1 before opening)"); return -1; }
-    const size_t cnt = (size_t)m->dargs.n_ph * m->sms * 4;
+    const size_t cnt = (size_t)m->dargs.n_ph * m->sms * kProfSlots;
     if (n < cnt) { set_err("profile buffer too small"); return -1; }
     cudaSetDevice(m->dev);
     if (cudaMemcpy(out, m->prof, cnt * 8, cudaMemcpyDeviceToHost) != cudaSuccess) { set_err("profile copy"); return -1; }

@@ -192,8 +192,11 @@ int fwb_trace_attn_read(fwb_model_t *m, uint64_t *out, size_t n);
 
 /*
  * Accumulated GEMV profile of the persistent kernel since the last read
- * (FWB_TRACE=1): out[(phase * n_sm + cta) * 4 + i] = ns that CTA spent in
- * i = 0 input prologue, 1 waiting for weight stages, 2 row loop, 3 tail.
+ * (FWB_TRACE=1), as seen by thread 0 of each CTA:
+ * out[(phase * n_sm + cta) * 8 + i] = ns spent in i = 0 input prologue,
+ * 1 waiting for the first weight stage, 2 row loop, 3 tail (loop end to phase
+ * end); from the phase start to 4 the first input loads landing, 5 the input
+ * planes' CTA barrier; 6 from its loop end until every warp's; 7 unused.
  * Resets the counters.  Returns the number of values written, or -1.
  */
 int fwb_prof_read(fwb_model_t *m, uint64_t *out, size_t n);
