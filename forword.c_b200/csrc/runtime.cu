@@ -25,6 +25,8 @@
 #include "tp_shard.h"
 #include "decode.cuh"
 #include "misc_kernels.cuh"
+#include "gemm_tc.cuh"
+#include "prefill.cuh"
 
 namespace fwb {
 
@@ -406,6 +408,12 @@ struct fwb_model {
     unsigned long long *gbase = nullptr;
     bool connected = false;
     unsigned long long *attn_trace = nullptr;  // FWB_TRACE: [layer][8] CTA 0's attention item timeline
+    // prompt path (fwb_prefill): scratch for kPrefillChunk tokens, allocated
+    // at the first call
+    uint32_t pf_cap = 0;
+    uint32_t *pf_tok = nullptr;
+    float *pf_x = nullptr, *pf_qkv = nullptr, *pf_q = nullptr, *pf_g = nullptr, *pf_u = nullptr;
+    __half *pf_h16 = nullptr, *pf_a16 = nullptr;
 };
 
 namespace fwb {
@@ -1142,6 +1150,54 @@ int quant_matvec_dev(const void *d_weights, size_t weights_size, uint32_t ggml_t
                : -1;
 }
 
+// Tensor-core dequant-GEMM launch (gemm_tc.cuh): Y[m][0..N) (row stride ldy)
+// = W X[m] for m < M, or += with TC_ADD.  Q4_0 with K a multiple of 64,
+// 4-byte-aligned weights and 16-byte-aligned fp16 activations only.
+static bool launch_tc_gemm(const void *w, size_t w_bytes, uint32_t type, const void *x, float *y, size_t K, size_t N,
+                           size_t M, size_t ldy, uint32_t mode, cudaStream_t st) {
+    static bool attr_set[64] = {};
+    if (!w || !x || !y || !K || !N || !M) { set_err("quant_gemm: null pointer or zero size"); return false; }
+    if (type != 2) { set_err("quant_gemm: only Q4_0 (type 2) runs on the tensor cores"); return false; }
+    if (K % kTcK) { set_err("quant_gemm: input size must be a multiple of 64"); return false; }
+    const size_t row_bytes = K / 32 * 18;
+    if (w_bytes < N * row_bytes) { set_err("quant_gemm: weights_size too small"); return false; }
+    if ((uintptr_t)w % 4 || (uintptr_t)x % 16 || ldy < N) { set_err("quant_gemm: misaligned operands"); return false; }
+    if (M > 65535u * kTcM || N > 0xffffffffu / 2) { set_err("quant_gemm: too many rows"); return false; }
+    int dev = 0;
+    CK(cudaGetDevice(&dev));
+    if (dev < 64 && !attr_set[dev]) {
+        CK(cudaFuncSetAttribute((const void *)gemm_q4_0_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)kTcSmem));
+        attr_set[dev] = true;
+    }
+    TcArgs a{};
+    a.w = static_cast<const uint8_t *>(w);
+    a.row_bytes = (uint32_t)row_bytes;
+    a.x = static_cast<const __half *>(x);
+    a.y = y;
+    a.M = (uint32_t)M;
+    a.N = (uint32_t)N;
+    a.K = (uint32_t)K;
+    a.ldy = (uint32_t)ldy;
+    a.mode = mode;
+    a.err = device_err_word(dev);
+    if (!a.err) { set_err("quant_gemm: device error word"); return false; }
+    const dim3 grid((unsigned)((N + kTcN - 1) / kTcN), (unsigned)((M + kTcM - 1) / kTcM));
+    gemm_q4_0_tc_kernel<<<grid, kTcThreads, kTcSmem, st>>>(a);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) { set_err(std::string("quant_gemm launch: ") + cudaGetErrorString(e)); return false; }
+    return true;
+}
+
+int quant_gemm_dev(const void *d_weights, size_t weights_size, uint32_t ggml_type, const void *d_input_f16,
+                   float *d_output, size_t input_size, size_t output_size, size_t n_tokens, int accumulate,
+                   void *stream) {
+    if (!launch_tc_gemm(d_weights, weights_size, ggml_type, d_input_f16, d_output, input_size, output_size, n_tokens,
+                        output_size, accumulate ? TC_ADD : TC_STORE, static_cast<cudaStream_t>(stream)))
+        return -1;
+    return 0;
+}
+
 int quant_dequant_dev(const void *d_weights, size_t weights_size, uint32_t ggml_type, float *d_out, size_t n_values,
                       void *stream) {
     uint32_t bb;
@@ -1276,6 +1332,105 @@ uint64_t fwb_model_weight_bytes(const fwb_model_t *m) { return m ? m->weight_byt
 int fwb_model_kernels_per_step(const fwb_model_t *m) {
     if (!m) return -1;
     return m->persistent ? 1 : (int)m->steps.size();
+}
+
+// The tensor-core prompt path needs every linear weight of the layers in
+// Q4_0 with a multiple of 64 inputs, head_dim <= 128 (a multiple of 4), one
+// GPU.  Other models take the per-token decode path for the prompt.
+static bool prefill_eligible(const fwb_model *m) {
+    const ModelConfig &c = m->cfg;
+    if (m->world != 1 || c.head_dim > 128 || c.head_dim % 4 || c.n_head % c.n_head_kv) return false;
+    for (const LayerW &w : m->layers)
+        for (const Mat *t : {&w.qkv, &w.o, &w.gate, &w.up, &w.down})
+            if (t->type != 2 || t->cols % kTcK || (uintptr_t)t->p % 4) return false;
+    return true;
+}
+
+constexpr uint32_t kPrefillChunk = 512;  // prompt tokens per pass through the layers
+
+static bool prefill_alloc(fwb_model *m) {
+    if (m->pf_cap) return true;
+    const ModelConfig &c = m->cfg;
+    const size_t C = kPrefillChunk, E = c.n_embd, F = c.n_ff, NQ = (size_t)c.n_head * c.head_dim;
+    const size_t NQKV = NQ + 2 * (size_t)c.n_head_kv * c.head_dim;
+    const size_t W16 = std::max({E, F, NQ});
+    if (!dalloc(m, (void **)&m->pf_tok, C * 4) || !dalloc(m, (void **)&m->pf_x, C * E * 4) ||
+        !dalloc(m, (void **)&m->pf_qkv, C * NQKV * 4) || !dalloc(m, (void **)&m->pf_q, C * NQ * 4) ||
+        !dalloc(m, (void **)&m->pf_g, C * F * 4) || !dalloc(m, (void **)&m->pf_u, C * F * 4) ||
+        !dalloc(m, (void **)&m->pf_h16, C * W16 * 2) || !dalloc(m, (void **)&m->pf_a16, C * NQ * 2))
+        return false;
+    m->pf_cap = (uint32_t)C;
+    return true;
+}
+
+// T prompt tokens (host array) at positions p0..p0+T-1 through every layer:
+// fills the KV cache; the residual stream after the last layer is not needed.
+static bool prefill_chunk(fwb_model *m, const uint32_t *tokens, uint32_t T, uint32_t p0) {
+    const ModelConfig &c = m->cfg;
+    const uint32_t E = c.n_embd, F = c.n_ff, hd = c.head_dim, H = c.n_head, KV = c.n_head_kv;
+    const uint32_t NQ = H * hd, NKV = KV * hd, NQKV = NQ + 2 * NKV;
+    const size_t layer_kv = (size_t)KV * m->kv_ctx * hd;
+    cudaStream_t st = m->st;
+    CK(cudaMemcpyAsync(m->pf_tok, tokens, (size_t)T * 4, cudaMemcpyHostToDevice, st));
+    pf_embed_kernel<<<T, 256, 0, st>>>(m->embd.p, m->embd.type, E, m->embd.row_bytes, m->pf_tok, m->pf_x);
+    const size_t att_smem = (size_t)(p0 + T) * 4;
+    if (att_smem > 48 * 1024)
+        CK(cudaFuncSetAttribute((const void *)pf_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)std::min<size_t>(att_smem, 200 * 1024)));
+    if (att_smem > 200 * 1024) { set_err("prefill: context too long for the attention scratch"); return false; }
+    for (uint32_t l = 0; l < c.n_layer; ++l) {
+        const LayerW &w = m->layers[l];
+        float *kc = m->kc + l * layer_kv, *vc = m->vc + l * layer_kv;
+        pf_rmsnorm_f16_kernel<<<T, 256, 0, st>>>(m->pf_x, w.attn_norm, c.norm_eps, E, m->pf_h16);
+        if (!launch_tc_gemm(w.qkv.p, (size_t)w.qkv.rows * w.qkv.row_bytes, 2, m->pf_h16, m->pf_qkv, E, NQKV, T, NQKV,
+                            TC_STORE, st))
+            return false;
+        pf_rope_kv_kernel<<<T, 256, 0, st>>>(m->pf_qkv, p0, NQ, NKV, hd, m->rope_cos, m->rope_sin, m->pf_q, kc, vc,
+                                             m->kv_ctx);
+        pf_attn_kernel<<<dim3(T, H), 128, att_smem, st>>>(m->pf_q, kc, vc, p0, H, H / KV, hd, m->kv_ctx,
+                                                         1.0f / sqrtf((float)hd), m->pf_a16);
+        if (l + 1 == c.n_layer) break;  // the last layer's output feeds only the logits
+        if (!launch_tc_gemm(w.o.p, (size_t)w.o.rows * w.o.row_bytes, 2, m->pf_a16, m->pf_x, NQ, E, T, E, TC_ADD, st))
+            return false;
+        pf_rmsnorm_f16_kernel<<<T, 256, 0, st>>>(m->pf_x, w.ffn_norm, c.norm_eps, E, m->pf_h16);
+        if (!launch_tc_gemm(w.gate.p, (size_t)w.gate.rows * w.gate.row_bytes, 2, m->pf_h16, m->pf_g, E, F, T, F,
+                            TC_STORE, st) ||
+            !launch_tc_gemm(w.up.p, (size_t)w.up.rows * w.up.row_bytes, 2, m->pf_h16, m->pf_u, E, F, T, F, TC_STORE,
+                            st))
+            return false;
+        pf_swiglu_kernel<<<std::min<size_t>(4096, ((size_t)T * F + 255) / 256), 256, 0, st>>>(
+            m->pf_g, m->pf_u, (size_t)T * F, m->pf_h16);
+        if (!launch_tc_gemm(w.down.p, (size_t)w.down.rows * w.down.row_bytes, 2, m->pf_h16, m->pf_x, F, E, T, E,
+                            TC_ADD, st))
+            return false;
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) { set_err(std::string("prefill launch: ") + cudaGetErrorString(e)); return false; }
+    return true;
+}
+
+int fwb_forward(fwb_model_t *m, uint32_t token, size_t pos, float *logits_host);
+
+int fwb_prefill(fwb_model_t *m, const uint32_t *tokens, size_t n, size_t pos0, float *logits_host) {
+    if (!m || !tokens || n == 0) { set_err("fwb_prefill: null model or tokens, or no tokens"); return -1; }
+    if (pos0 + n > m->kv_ctx) { set_err("fwb_prefill: positions exceed the KV cache"); return -1; }
+    for (size_t i = 0; i < n; ++i)
+        if (tokens[i] >= m->cfg.n_vocab) { set_err("fwb_prefill: token ID out of range"); return -1; }
+    cudaSetDevice(m->dev);
+    const char *env = getenv("FWB_PREFILL_PER_TOKEN");
+    const bool batched = n > 1 && prefill_eligible(m) && !(env && *env == '1');
+    if (!batched) {  // the decode path, one token after the other (as main.c does)
+        for (size_t i = 0; i + 1 < n; ++i)
+            if (fwb_forward(m, tokens[i], pos0 + i, nullptr) != 0) return -1;
+    } else {
+        if (!prefill_alloc(m)) return -1;
+        for (size_t i = 0; i + 1 < n; i += kPrefillChunk) {
+            const uint32_t T = (uint32_t)std::min<size_t>(kPrefillChunk, n - 1 - i);
+            if (!prefill_chunk(m, tokens + i, T, (uint32_t)(pos0 + i))) return -1;
+        }
+    }
+    // the last token through the decode step gives the logits
+    return fwb_forward(m, tokens[n - 1], pos0 + n - 1, logits_host);
 }
 
 int fwb_forward(fwb_model_t *m, uint32_t token, size_t pos, float *logits_host) {

@@ -94,6 +94,16 @@ class Model:
             raise FwbError(f"fwb_forward: {_err(self.lib)}")
         return dst.copy() if out is None else dst
 
+    def prefill(self, tokens, pos0: int = 0) -> np.ndarray:
+        """fwb_prefill: feed tokens at pos0.. and return the last token's logits."""
+        tok = np.ascontiguousarray(tokens, dtype=np.uint32)
+        out = np.zeros(self.n_vocab, dtype=np.float32)
+        rc = self.lib.fwb_prefill(self.h, tok.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)), tok.size, pos0,
+                                  out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)))
+        if rc != 0:
+            raise FwbError(f"fwb_prefill: {_err(self.lib)}")
+        return out
+
     def try_forward(self, token: int, pos: int) -> int:
         """Raw return code of fwb_forward (0 / -1) for error-path tests."""
         return int(self.lib.fwb_forward(self.h, token, pos, None))

@@ -66,11 +66,13 @@ def _declare(lib) -> None:
     sig("fwb_device_count", _i32)
     sig("quant_matvec", _i32, _vp, _sz, _u32, _fp, _fp, _sz, _sz)
     sig("quant_matvec_dev", _i32, _vp, _sz, _u32, _vp, _vp, _sz, _sz, _vp)
+    sig("quant_gemm_dev", _i32, _vp, _sz, _u32, _vp, _vp, _sz, _sz, _sz, _i32, _vp)
     sig("quant_dequant_dev", _i32, _vp, _sz, _u32, _vp, _sz, _vp)
     sig("fwb_model_open", _vp, _c.c_char_p, _sz, _i32)
     sig("fwb_model_close", None, _vp)
     sig("fwb_model_dims", _i32, _vp, _c.POINTER(_u32))
     sig("fwb_forward", _i32, _vp, _u32, _sz, _fp)
+    sig("fwb_prefill", _i32, _vp, _c.POINTER(_u32), _sz, _sz, _c.POINTER(_c.c_float))
     sig("fwb_forward_argmax", _i32, _vp, _u32, _sz, _c.POINTER(_u32))
     sig("fwb_kv_load", _i32, _vp, _sz, _sz, _sz, _fp, _fp)
     sig("fwb_kv_read", _i32, _vp, _sz, _sz, _sz, _fp, _fp)

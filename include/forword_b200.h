@@ -101,6 +101,20 @@ int quant_matvec_dev(const void *d_weights, size_t weights_size, uint32_t ggml_t
                      size_t output_size, void *stream);
 
 /*
+ * Batched (prompt) form of quant_matvec_dev on the tensor cores:
+ * output[m * output_size + o] = sum_k W[o][k] * input[m * input_size + k] for
+ * m < n_tokens (or += with accumulate != 0).  d_input_f16 holds fp16
+ * activations (16-byte aligned); the products are accumulated in fp32.  This
+ * is the dense contraction of a prompt's tokens sharing each weight tile, the
+ * batched counterpart of linear_forward (linear.c:155-223), which the
+ * reference only runs one token at a time.  Only Q4_0 (type 2) with
+ * input_size a multiple of 64; other cases return -1.  Asynchronous.
+ */
+int quant_gemm_dev(const void *d_weights, size_t weights_size, uint32_t ggml_type, const void *d_input_f16,
+                   float *d_output, size_t input_size, size_t output_size, size_t n_tokens, int accumulate,
+                   void *stream);
+
+/*
  * Dequantise n_values (a multiple of 32) from Q4_0 / Q5_0 / Q8_0 blocks into
  * fp32 on the device, bit-identical to the reference decoders (q8_0_decode
  * quant.c:232-263, q5_0_decode linear.c:40-56, and GGML's Q4_0).
@@ -142,6 +156,21 @@ int fwb_model_kernels_per_step(const fwb_model_t *m);
  * token_id >= n_vocab -> -1.
  */
 int fwb_forward(fwb_model_t *m, uint32_t token_id, size_t pos, float *logits_host);
+
+/*
+ * Prompt processing: feed tokens[0..n) at positions pos0..pos0+n-1, as n
+ * calls of fwb_forward would (main.c:145-151 feeds a prompt that way), and
+ * write the logits of the last token to logits_host (may be NULL).  The first
+ * n-1 tokens go through every layer together: their linear layers run as
+ * dequant-GEMMs on the tensor cores (see quant_gemm_dev) with fp16
+ * activations, and their K/V rows are appended to the cache; the last token
+ * takes the decode step.  Models whose layer weights are not all Q4_0 (or
+ * with an input width that is not a multiple of 64, or head_dim > 128, or
+ * tensor parallelism) take the decode step for every token.  Set
+ * FWB_PREFILL_PER_TOKEN=1 to force that path.  -1 (with fwb_last_error()) for
+ * positions beyond the KV cache or token ids beyond the vocabulary.
+ */
+int fwb_prefill(fwb_model_t *m, const uint32_t *tokens, size_t n, size_t pos0, float *logits_host);
 
 /* Same step, returning only the greedy next token (sampler_argmax,
  * sampler.c:28-32: the lowest index among equal maxima). */
