@@ -311,10 +311,28 @@ def run_b200(args) -> None:
     m = tp.open_model(path, kv_ctx, rank, world, local) if world > 1 else Model(path, max_ctx=kv_ctx, device=local)
     stream = torch.cuda.ExternalStream(m.stream, device=torch.device(f"cuda:{local}"))
 
-    # prompt: one forward per token (teacher forced), as the reference's main loop
-    tok = 0
-    for i, t in enumerate(wl.prompt_ids()):
-        tok = m.forward_argmax(int(t), i)
+    # prompt.  One GPU: fwb_prefill (the prompt's tokens through each layer
+    # together on the tensor cores), once to warm up (scratch allocation) and
+    # once timed; tensor parallel: one forward per token, as the reference's
+    # main loop.
+    prefill = None
+    prompt = wl.prompt_ids()
+    if world == 1:
+        m.prefill(prompt, 0)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        logits = m.prefill(prompt, 0)
+        pf_s = time.perf_counter() - t0
+        tok = int(np.argmax(logits))
+        flops = 2.0 * wl.cfg.prefill_gemm_params() * (P - 1)
+        prefill = {"tokens": P, "ms": pf_s * 1e3, "tokens_per_s": P / pf_s,
+                   "gemm_tflops": flops / pf_s / 1e12,
+                   "api": "fwb_prefill with host tokens and the last token's host logits (wall clock): "
+                          "P-1 tokens through the tensor-core dequant-GEMM path, the last through the decode step"}
+    else:
+        tok = 0
+        for i, t in enumerate(prompt):
+            tok = m.forward_argmax(int(t), i)
     pos = P
 
     # warm-up
@@ -403,6 +421,8 @@ def run_b200(args) -> None:
             "clocks": clk,
             "gpu_launches": kernels * K,
         }
+        if prefill:
+            line["prefill"] = prefill
         if wl.tp:
             line["roofline"]["note"] = ("per GPU: its weight slices; the box-wide tokens/s is the value "
                                         "(one decode stream across all GPUs)")

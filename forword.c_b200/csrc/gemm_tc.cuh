@@ -14,7 +14,8 @@
 // decoders, then rounded to fp16) into shared memory in the K-major 128-byte
 // swizzled layout the MMA reads; one thread issues four
 // tcgen05.mma.kind::f16 (K = 16 each) and commits them to an mbarrier.  Two
-// stages: the loads of step i+1 overlap the MMAs of step i.  The epilogue
+// stages: the loads of step i+1 overlap the MMAs of step i, and each thread
+// has step i+1's global bytes in flight while it writes step i's tiles.  The epilogue
 // reads the accumulator with tcgen05.ld (warp w owns TMEM lanes 32w..32w+31)
 // and stores, or adds into, Y.
 //
@@ -97,71 +98,74 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
     return *reinterpret_cast<const uint32_t *>(&h);
 }
 
-// One stage: this thread's activation row and weight row into the swizzled
-// A / B tiles (rows outside M / N are zero).
-__device__ __forceinline__ void tc_load_stage(const TcArgs &a, uint8_t *sa, uint8_t *sb, uint32_t m0, uint32_t n0,
-                                              uint32_t k0) {
-    const uint32_t t = threadIdx.x;
-    {  // activations: 64 fp16 = 8 chunks
-        const uint32_t m = m0 + t;
-        uint4 c[8];
-        if (m < a.M) {
-            const uint4 *src = reinterpret_cast<const uint4 *>(a.x + (size_t)m * a.K + k0);
+// The global bytes of one stage for this thread: its activation row (64 fp16)
+// and its weight row's two Q4_0 blocks (36 bytes, 4-byte aligned).  Fetched
+// one stage ahead so that their latency hides behind the current stage.
+struct TcRaw {
+    uint4 a[8];
+    uint32_t q[9];
+};
+
+__device__ __forceinline__ void tc_fetch(const TcArgs &a, uint32_t m0, uint32_t n0, uint32_t k0, TcRaw &r) {
+    const uint32_t t = threadIdx.x, m = m0 + t, n = n0 + t;
+    if (m < a.M) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(a.x + (size_t)m * a.K + k0);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) c[i] = __ldg(src + i);
-        } else {
+        for (int i = 0; i < 8; ++i) r.a[i] = __ldg(src + i);
+    } else {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) c[i] = make_uint4(0u, 0u, 0u, 0u);
-        }
-#pragma unroll
-        for (uint32_t i = 0; i < 8; ++i) *reinterpret_cast<uint4 *>(sa + tc_sw128(t, i)) = c[i];
+        for (int i = 0; i < 8; ++i) r.a[i] = make_uint4(0u, 0u, 0u, 0u);
     }
-    {  // weights: two Q4_0 blocks (36 bytes, 4-byte aligned) -> 64 fp16
-        const uint32_t n = n0 + t;
-        uint32_t q[9];
-        if (n < a.N) {
-            const uint32_t *src = reinterpret_cast<const uint32_t *>(a.w + (size_t)n * a.row_bytes + (k0 >> 5) * 18u);
+    if (n < a.N) {
+        const uint32_t *src = reinterpret_cast<const uint32_t *>(a.w + (size_t)n * a.row_bytes + (k0 >> 5) * 18u);
 #pragma unroll
-            for (int i = 0; i < 9; ++i) q[i] = __ldg(src + i);
-        } else {
+        for (int i = 0; i < 9; ++i) r.q[i] = __ldg(src + i);
+    } else {
 #pragma unroll
-            for (int i = 0; i < 9; ++i) q[i] = 0u;  // d = 0: every value 0
-        }
-        // block 0: d in q[0] low half, quants in bytes 2..17; block 1: d in q[4]
-        // high half, quants in bytes 20..35 = q[5..8]
-        const float d0 = __half2float(__ushort_as_half((unsigned short)(q[0] & 0xffffu)));
-        const float d1 = __half2float(__ushort_as_half((unsigned short)(q[4] >> 16)));
-        uint32_t qs0[4], qs1[4];
+        for (int i = 0; i < 9; ++i) r.q[i] = 0u;  // d = 0: every value 0
+    }
+}
+
+// One stage into the swizzled A / B tiles: the activation row as is, the
+// weight row dequantised (rows outside M / N are zero).
+__device__ __forceinline__ void tc_store_stage(const TcRaw &r, uint8_t *sa, uint8_t *sb) {
+    const uint32_t t = threadIdx.x;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            qs0[i] = __funnelshift_r(q[i], q[i + 1], 16);
-            qs1[i] = q[5 + i];
-        }
+    for (uint32_t i = 0; i < 8; ++i) *reinterpret_cast<uint4 *>(sa + tc_sw128(t, i)) = r.a[i];
+    // block 0: d in q[0] low half, quants in bytes 2..17; block 1: d in q[4]
+    // high half, quants in bytes 20..35 = q[5..8]
+    const float d0 = __half2float(__ushort_as_half((unsigned short)(r.q[0] & 0xffffu)));
+    const float d1 = __half2float(__ushort_as_half((unsigned short)(r.q[4] >> 16)));
+    uint32_t qs0[4], qs1[4];
 #pragma unroll
-        for (uint32_t blk = 0; blk < 2; ++blk) {
-            const uint32_t *qs = blk ? qs1 : qs0;
-            const float d = blk ? d1 : d0;
-            // element j (< 16): low nibble of byte j; element j + 16: high nibble
+    for (int i = 0; i < 4; ++i) {
+        qs0[i] = __funnelshift_r(r.q[i], r.q[i + 1], 16);
+        qs1[i] = r.q[5 + i];
+    }
 #pragma unroll
-            for (uint32_t half = 0; half < 2; ++half) {
+    for (uint32_t blk = 0; blk < 2; ++blk) {
+        const uint32_t *qs = blk ? qs1 : qs0;
+        const float d = blk ? d1 : d0;
+        // element j (< 16): low nibble of byte j; element j + 16: high nibble
 #pragma unroll
-                for (uint32_t cc = 0; cc < 2; ++cc) {  // 8 elements per chunk
-                    uint32_t o[4];
+        for (uint32_t half = 0; half < 2; ++half) {
 #pragma unroll
-                    for (uint32_t e = 0; e < 4; ++e) {
-                        float v[2];
+            for (uint32_t cc = 0; cc < 2; ++cc) {  // 8 elements per chunk
+                uint32_t o[4];
 #pragma unroll
-                        for (uint32_t u = 0; u < 2; ++u) {
-                            const uint32_t j = cc * 8 + e * 2 + u;  // byte index 0..15
-                            const uint32_t byte = (qs[j >> 2] >> ((j & 3) * 8)) & 0xffu;
-                            const int qv = (int)(half ? (byte >> 4) : (byte & 15u)) - 8;
-                            v[u] = __fmul_rn((float)qv, d);
-                        }
-                        o[e] = pack_h2(v[0], v[1]);
+                for (uint32_t e = 0; e < 4; ++e) {
+                    float v[2];
+#pragma unroll
+                    for (uint32_t u = 0; u < 2; ++u) {
+                        const uint32_t j = cc * 8 + e * 2 + u;  // byte index 0..15
+                        const uint32_t byte = (qs[j >> 2] >> ((j & 3) * 8)) & 0xffu;
+                        const int qv = (int)(half ? (byte >> 4) : (byte & 15u)) - 8;
+                        v[u] = __fmul_rn((float)qv, d);
                     }
-                    const uint32_t chunk = blk * 4 + half * 2 + cc;
-                    *reinterpret_cast<uint4 *>(sb + tc_sw128(t, chunk)) = make_uint4(o[0], o[1], o[2], o[3]);
+                    o[e] = pack_h2(v[0], v[1]);
                 }
+                const uint32_t chunk = blk * 4 + half * 2 + cc;
+                *reinterpret_cast<uint4 *>(sb + tc_sw128(t, chunk)) = make_uint4(o[0], o[1], o[2], o[3]);
             }
         }
     }
@@ -194,12 +198,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q4_0_tc_kernel(const __gri
 
     const uint32_t steps = a.K / kTcK;
     bool ok = true;
+    TcRaw raw;
+    if (steps > 0) tc_fetch(a, m0, n0, 0, raw);
     for (uint32_t it = 0; it < steps; ++it) {
         const uint32_t s = it & 1u;
         uint8_t *sa = smem + s * 2u * kTcTileBytes, *sb = sa + kTcTileBytes;  // stage s: A then B
+        TcRaw next = raw;
+        if (it + 1 < steps) tc_fetch(a, m0, n0, (it + 1) * kTcK, next);
         if (it >= 2 && ok)  // the MMAs that read this stage two steps ago are done
             ok = mbar_wait(&bar[s], ((it - 2) >> 1) & 1u, a.err, ERR_WAIT_FULL);
-        tc_load_stage(a, sa, sb, m0, n0, it * kTcK);
+        tc_store_stage(raw, sa, sb);
+        raw = next;
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core reads
         __syncthreads();
         if (tid == 0) {

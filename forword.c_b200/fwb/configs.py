@@ -65,6 +65,14 @@ class ModelShape:
         embd_row = self.tensor_bytes(self.t_embd, 1, E)
         return self.n_layer * per_layer + head + E * 4 + embd_row
 
+    def prefill_gemm_params(self) -> int:
+        """Weights one prompt token multiplies in the prompt path's GEMMs
+        (fwb_prefill): QKV in every layer, o-proj and the FFN in all but the
+        last (whose output only feeds the logits).  FLOPs = 2 x this."""
+        E, F, hd = self.n_embd, self.n_ff, self.head_dim
+        q, kv = self.n_head * hd, self.n_head_kv * hd
+        return self.n_layer * (q + 2 * kv) * E + (self.n_layer - 1) * (q * E + 3 * E * F)
+
     def kv_bytes_per_token(self, n_pos: int) -> int:
         """fp32 K and V bytes the attention of one decode step reads at n_pos
         cached positions (all layers)."""
