@@ -79,7 +79,7 @@ struct DecodeArgs {
     uint32_t total_st;     // stages per CTA (max over CTAs is fine: CTAs read their own table)
     uint32_t NS, stage_bytes, scratch_bytes;
     const uint32_t *step;  // [0] token, [1] position of this step
-    uint32_t *sync;        // [0] barrier arrivals (zeroed before each launch), [1] abort
+    uint32_t *sync;        // [0] barrier arrivals, [1] abort, [2] cross-rank barriers passed (zeroed before each launch)
     uint32_t *err;
     uint32_t *n_st_cta;    // [gridDim.x] stages of each CTA
     // tensor parallelism (world > 1): cross-rank barrier counters (every rank's,
@@ -214,23 +214,39 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys64(const unsigned lo
     return v;
 }
 
-// Barrier across every CTA of every rank (tensor parallelism): each CTA adds
-// one to every rank's counter (release, system scope: its writes of the phase
-// become visible to the peers) and waits (acquire) until its own counter shows
-// all world * gridDim.x arrivals of barrier `target / (world * gridDim.x)`.
-// Bounded like grid_sync; a timeout sets the local abort flag and the error.
-__device__ bool global_sync(const DecodeArgs &d, unsigned long long target) {
+// Barrier across every CTA of every rank (tensor parallelism), after this
+// rank's own grid barrier: CTA 0 alone adds one to every rank's counter
+// (release, system scope: after the grid barrier before it, every local CTA's
+// writes of the phase are covered and become visible to the peers) and waits
+// (acquire) until its own counter shows all `world` arrivals of barrier
+// number `nb` (counted across launches); it then publishes `gk` (this
+// launch's count of such barriers) in sync[2], which the other CTAs wait for
+// (acquire).  One system-scope atomic per rank and barrier instead of one per
+// CTA.  Bounded like grid_sync; a timeout sets the local abort flag and the
+// error.
+__device__ bool global_sync(const DecodeArgs &d, unsigned long long nb, uint32_t gk) {
     __shared__ uint32_t ok_flag;
-    __syncthreads();
     if (threadIdx.x == 0) {
-        for (uint32_t q = 0; q < d.world; ++q) red_release_sys_add64(d.gcount[q], 1ull);
-        const unsigned long long *mine = d.gcount[0];
         uint32_t ok = 0;
-        for (uint32_t i = 0; i < (1u << 25); ++i) {
-            if (ld_acquire_sys64(mine) >= target) { ok = 1; break; }
-            if ((i & 255) == 255) {
-                if (ld_acquire(&d.sync[1])) break;
-                __nanosleep(64);
+        if (blockIdx.x == 0) {
+            for (uint32_t q = 0; q < d.world; ++q) red_release_sys_add64(d.gcount[q], 1ull);
+            const unsigned long long *mine = d.gcount[0];
+            const unsigned long long target = nb * d.world;
+            for (uint32_t i = 0; i < (1u << 25); ++i) {
+                if (ld_acquire_sys64(mine) >= target) { ok = 1; break; }
+                if ((i & 255) == 255) {
+                    if (ld_acquire(&d.sync[1])) break;
+                    __nanosleep(64);
+                }
+            }
+            if (ok) st_release_gpu(&d.sync[2], gk);
+        } else {
+            for (uint32_t i = 0; i < (1u << 25); ++i) {
+                if (ld_acquire(&d.sync[2]) >= gk) { ok = 1; break; }
+                if ((i & 255) == 255) {
+                    if (ld_acquire(&d.sync[1])) break;
+                    __nanosleep(32);
+                }
             }
         }
         if (!ok) {
@@ -429,16 +445,14 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
         // (the barriers' leading __syncthreads makes the copied descriptor visible)
         if (next) {
             const Phase &N = ph_buf[(p + 1) & 1];
-            // a phase after a cross-rank barrier is preceded by that barrier only:
-            // it includes every local CTA, so the local count is advanced too
-            // (grid_sync counts epochs by phase index)
+            // a phase after a cross-rank barrier is preceded by this rank's grid
+            // barrier and then the cross-rank one (grid_sync counts epochs by
+            // phase index)
             __syncthreads();
+            if (!grid_sync(d.sync, p + 1, d.err, &N, pos)) ok = false;
             if (N.gsync) {
                 ++gk;
-                if (!global_sync(d, (gbase + gk) * (unsigned long long)d.world * gridDim.x)) ok = false;
-                if (tid == 0) red_release_add(&d.sync[0], 1u);
-            } else if (!grid_sync(d.sync, p + 1, d.err, &N, pos)) {
-                ok = false;
+                if (!global_sync(d, gbase + gk, gk)) ok = false;
             }
         }
     }

@@ -1014,7 +1014,7 @@ static bool build_decode(fwb_model *m) {
 }
 
 static cudaError_t launch_decode(fwb_model *m) {
-    cudaError_t e = cudaMemsetAsync(m->sync, 0, 8, m->st);
+    cudaError_t e = cudaMemsetAsync(m->sync, 0, 16, m->st);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(m->sms);
