@@ -157,3 +157,23 @@ def test_full_width_layers_vs_oracle(gpu, model_dir, cfg):
     assert not mism, f"greedy mismatches: {mism}"
     print(f"{cfg.name}: worst max-abs {wa:.3g} rel {wr:.3g} min gap {gap:.3g}")
     assert wa <= 1e-2 and wr <= 1e-3
+
+
+def test_long_context_more_than_32_splits_vs_oracle(gpu, model_dir):
+    """Two KV heads and 3000 pre-filled positions: the attention splits each
+    head over more than 32 CTAs (the merge's second round of loads)."""
+    cfg = dataclasses.replace(configs.SMALL_Q4_0, name="small-q4_0-ctx4k", n_ctx=4096)
+    path = _model_path(model_dir, cfg, 302)
+    orc = pyoracle.OracleModel(path, max_ctx=cfg.n_ctx)
+    pos0 = 3000
+    with Model(path, max_ctx=cfg.n_ctx) as m:
+        rng = np.random.default_rng(6)
+        for layer in range(cfg.n_layer):
+            shape = (pos0, cfg.n_head_kv, cfg.head_dim)
+            k = rng.standard_normal(shape).astype(np.float32)
+            v = rng.standard_normal(shape).astype(np.float32)
+            m.kv_load(layer, 0, k, v)
+            orc.kv_load(layer, 0, k, v)
+        mism, wa, wr, gap = greedy_compare(m.forward, orc.forward, 5, pos0, 4)
+    assert not mism, f"greedy mismatches: {mism}"
+    assert wa <= 1e-2 and wr <= 1e-3
