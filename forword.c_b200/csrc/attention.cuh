@@ -41,7 +41,7 @@ __device__ __forceinline__ void attn_stamp(const AttnArgs &a, int i) {
 }
 
 constexpr int kAttnWarps = 4;          // warps per CTA of the standalone kernel
-constexpr uint32_t kMinSplitPos = 64;   // positions per split at least
+constexpr uint32_t kMinSplitPos = 32;   // positions per split at least
 constexpr uint32_t kMaxSplits = 64;
 
 // Splits in use at n_pos positions (short contexts merge few partials).
