@@ -146,6 +146,85 @@ __global__ void pf_attn_kernel(const float *qf, const float *kcache, const float
     }
 }
 
+// The same attention for all GQ query heads of one KV head per block (grid
+// (T, n_kv), 128 threads, hd <= 128): each K row is read once for the GQ
+// heads and each V row once for GQ outputs; positions are split over the
+// four warps in both passes.  Scores of head g at pf_sc2[g * n_pos + i].
+template <int GQ>
+__global__ void pf_attn_gqa_kernel(const float *qf, const float *kcache, const float *vcache, uint32_t p0,
+                                   uint32_t n_head, uint32_t hd, uint32_t kv_ctx, float scale, __half *out) {
+    extern __shared__ float pf_sc2[];  // [GQ][positions]
+    __shared__ float red[32];
+    const uint32_t t = blockIdx.x, kvh = blockIdx.y;
+    const uint32_t n_pos = p0 + t + 1;
+    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const uint32_t nq = n_head * hd;
+    const float *kb = kcache + (size_t)kvh * kv_ctx * hd, *vb = vcache + (size_t)kvh * kv_ctx * hd;
+    const bool act = 4 * lane < hd;
+    float4 qv[GQ];
+#pragma unroll
+    for (int g = 0; g < GQ; ++g)
+        qv[g] = act ? *reinterpret_cast<const float4 *>(qf + (size_t)t * nq + (size_t)(kvh * GQ + g) * hd + 4 * lane)
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (uint32_t i = warp; i < n_pos; i += nw) {
+        const float4 k = act ? __ldg(reinterpret_cast<const float4 *>(kb + (size_t)i * hd + 4 * lane))
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int g = 0; g < GQ; ++g) {
+            float dot = fmaf(qv[g].w, k.w, fmaf(qv[g].z, k.z, fmaf(qv[g].y, k.y, qv[g].x * k.x)));
+#pragma unroll
+            for (int o = 16; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+            if (lane == 0) pf_sc2[g * n_pos + i] = __fmul_rn(dot, scale);
+        }
+    }
+    __syncthreads();
+    for (int g = 0; g < GQ; ++g) {  // softmax of head g (attention.c:18-33)
+        float *sc = pf_sc2 + g * n_pos;
+        float m = -INFINITY;
+        for (uint32_t i = threadIdx.x; i < n_pos; i += blockDim.x) m = fmaxf(m, sc[i]);
+        m = pf_block_max(m, red);
+        float s = 0.f;
+        for (uint32_t i = threadIdx.x; i < n_pos; i += blockDim.x) {
+            const float e = expf(sc[i] - m);
+            sc[i] = e;
+            s += e;
+        }
+        s = pf_block_sum(s, red);
+        const float inv = __fdiv_rn(1.0f, s);
+        if (s > 0.0f && isfinite(s))
+            for (uint32_t i = threadIdx.x; i < n_pos; i += blockDim.x) sc[i] = __fmul_rn(sc[i], inv);
+    }
+    __syncthreads();
+    // weighted sum of the value rows: warp w takes positions w, w + nw, ...
+    // (lanes own 4 dims each), then the warps' partial sums are added
+    __shared__ float part[4][GQ][128];
+    float4 acc[GQ];
+#pragma unroll
+    for (int g = 0; g < GQ; ++g) acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (uint32_t i = warp; i < n_pos; i += nw) {
+        const float4 v = act ? __ldg(reinterpret_cast<const float4 *>(vb + (size_t)i * hd + 4 * lane))
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int g = 0; g < GQ; ++g) {
+            const float p = pf_sc2[g * n_pos + i];
+            acc[g].x = fmaf(p, v.x, acc[g].x);
+            acc[g].y = fmaf(p, v.y, acc[g].y);
+            acc[g].z = fmaf(p, v.z, acc[g].z);
+            acc[g].w = fmaf(p, v.w, acc[g].w);
+        }
+    }
+    if (act)
+#pragma unroll
+        for (int g = 0; g < GQ; ++g) *reinterpret_cast<float4 *>(&part[warp][g][4 * lane]) = acc[g];
+    __syncthreads();
+    for (uint32_t j = threadIdx.x; j < GQ * hd; j += blockDim.x) {
+        const uint32_t g = j / hd, d = j % hd;
+        float o = 0.f;
+        for (uint32_t w = 0; w < nw; ++w) o += part[w][g][d];
+        out[(size_t)t * nq + (size_t)(kvh * GQ + g) * hd + d] = __float2half_rn(o);
+    }
+}
+
 // h = fp16(silu(gate) * up) (ffn.c:17-25, 90-106)
 __global__ void pf_swiglu_kernel(const float *g, const float *u, size_t n, __half *h) {
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {

@@ -1363,6 +1363,35 @@ static bool prefill_alloc(fwb_model *m) {
     return true;
 }
 
+// Prompt attention: all query heads of a KV head per block when their scores
+// fit in shared memory (GQ 1, 2, 4 or 8), else one block per query head.
+static bool launch_pf_attn(fwb_model *m, const float *kc, const float *vc, uint32_t T, uint32_t p0,
+                           size_t att_smem, cudaStream_t st) {
+    const ModelConfig &c = m->cfg;
+    const uint32_t H = c.n_head, KV = c.n_head_kv, hd = c.head_dim, gq = H / KV;
+    const float scale = 1.0f / sqrtf((float)hd);
+    const size_t smem_g = att_smem * gq;
+    auto run = [&](const void *fn) -> bool {
+        if (smem_g > 48 * 1024)
+            CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_g));
+        void *args[] = {(void *)&m->pf_q, (void *)&kc, (void *)&vc, (void *)&p0, (void *)&H,
+                        (void *)&hd, (void *)&m->kv_ctx, (void *)&scale, (void *)&m->pf_a16};
+        CK(cudaLaunchKernel(fn, dim3(T, KV), dim3(128), args, smem_g, st));
+        return true;
+    };
+    if (smem_g <= 200 * 1024) {
+        switch (gq) {
+        case 1: return run((const void *)pf_attn_gqa_kernel<1>);
+        case 2: return run((const void *)pf_attn_gqa_kernel<2>);
+        case 4: return run((const void *)pf_attn_gqa_kernel<4>);
+        case 8: return run((const void *)pf_attn_gqa_kernel<8>);
+        default: break;
+        }
+    }
+    pf_attn_kernel<<<dim3(T, H), 128, att_smem, st>>>(m->pf_q, kc, vc, p0, H, gq, hd, m->kv_ctx, scale, m->pf_a16);
+    return true;
+}
+
 // T prompt tokens (host array) at positions p0..p0+T-1 through every layer:
 // fills the KV cache; the residual stream after the last layer is not needed.
 static bool prefill_chunk(fwb_model *m, const uint32_t *tokens, uint32_t T, uint32_t p0) {
@@ -1387,8 +1416,7 @@ static bool prefill_chunk(fwb_model *m, const uint32_t *tokens, uint32_t T, uint
             return false;
         pf_rope_kv_kernel<<<T, 256, 0, st>>>(m->pf_qkv, p0, NQ, NKV, hd, m->rope_cos, m->rope_sin, m->pf_q, kc, vc,
                                              m->kv_ctx);
-        pf_attn_kernel<<<dim3(T, H), 128, att_smem, st>>>(m->pf_q, kc, vc, p0, H, H / KV, hd, m->kv_ctx,
-                                                         1.0f / sqrtf((float)hd), m->pf_a16);
+        if (!launch_pf_attn(m, kc, vc, T, p0, att_smem, st)) return false;
         if (l + 1 == c.n_layer) break;  // the last layer's output feeds only the logits
         if (!launch_tc_gemm(w.o.p, (size_t)w.o.rows * w.o.row_bytes, 2, m->pf_a16, m->pf_x, NQ, E, T, E, TC_ADD, st))
             return false;
