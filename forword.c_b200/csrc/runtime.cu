@@ -396,6 +396,7 @@ struct fwb_model {
     unsigned long long *prof = nullptr;  // [n_phases][G][kProfSlots] GEMV profile (FWB_TRACE=1)
     fwb::DecodeArgs dargs{};
     size_t dsmem = 0;
+    const void *decode_fn = nullptr;  // the persistent kernel's specialisation for this model
     uint32_t *sync = nullptr;
     std::vector<void *> allocs;
     // tensor parallelism (world > 1): this rank's exchange buffer, every
@@ -925,8 +926,20 @@ static bool build_decode(fwb_model *m) {
                                                 (nw * 32 + 3 * nw * gq + nw * gq * hd + gq + gq * kMaxSplits + gq + 1) * 4);
         scratch = std::max(scratch, (att + 127) / 128 * 128);
     }
+    // the specialisation of the persistent kernel for this model's phases
+    {
+        bool q4a4 = true;
+        for (const Phase &p : ph)
+            if (p.kind == PH_GEMV && (p.qt != QT_Q4_0 || !p.a4)) q4a4 = false;
+        const uint32_t hd = m->cfg.head_dim, gq = m->cfg.n_head / m->cfg.n_head_kv;
+        m->decode_fn = (const void *)decode_kernel_t<0, 0, 0>;
+        if (q4a4 && hd == 128 && gq == 4) m->decode_fn = (const void *)decode_kernel_t<1, 128, 4>;
+        if (q4a4 && hd == 128 && gq == 8) m->decode_fn = (const void *)decode_kernel_t<1, 128, 8>;
+        const char *gen = getenv("FWB_GENERIC_KERNEL");
+        if (gen && *gen == '1') m->decode_fn = (const void *)decode_kernel_t<0, 0, 0>;
+    }
     cudaFuncAttributes fa;
-    CK(cudaFuncGetAttributes(&fa, (const void *)decode_kernel));
+    CK(cudaFuncGetAttributes(&fa, m->decode_fn));
     const size_t tab_bytes = (size_t)n_ph * sizeof(StageSrc);
     const size_t fixed = kHeaderBytes + scratch + 128 + tab_bytes + fa.sharedSizeBytes + 1024;
     if (fixed + 2 * (size_t)stage > kMaxSmem) { set_err("persistent kernel: shared memory too small"); return false; }
@@ -1006,9 +1019,9 @@ static bool build_decode(fwb_model *m) {
             return false;
     }
     m->dsmem = kHeaderBytes + scratch + (size_t)ns * stage + 128 + tab_bytes;
-    CK(cudaFuncSetAttribute((const void *)decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->dsmem));
+    CK(cudaFuncSetAttribute(m->decode_fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->dsmem));
     int per_sm = 0;
-    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, (const void *)decode_kernel, kDecodeThreads, m->dsmem));
+    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, m->decode_fn, kDecodeThreads, m->dsmem));
     if (per_sm < 1) { set_err("persistent kernel does not fit on an SM"); return false; }
     return true;
 }
@@ -1028,7 +1041,7 @@ static cudaError_t launch_decode(fwb_model *m) {
     cfg.numAttrs = 1;
     DecodeArgs d = m->dargs;
     void *args[] = {&d};
-    return cudaLaunchKernelExC(&cfg, (const void *)decode_kernel, args);
+    return cudaLaunchKernelExC(&cfg, m->decode_fn, args);
 }
 
 static bool run_steps(fwb_model *m) {
