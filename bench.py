@@ -75,8 +75,9 @@ class Workload:
         self.cfg = configs.LLAMA70B_Q4_0 if self.tp else configs.LLAMA8B_Q4_0
         self.prompt = 256 if self.tp else 512
         shape = "Llama-70B" if self.tp else "Llama-3-8B"
+        feed = "one decode step per token" if self.tp else "fwb_prefill"
         self.text = (f"{shape}-shaped decoder, all linear weights Q4_0, fp32 embedding/norms, "
-                     f"random-init N(0,0.02); {self.prompt}-token random prompt fed per token, then "
+                     f"random-init N(0,0.02); {self.prompt}-token random prompt ({feed}), then "
                      f"greedy decode at batch 1" + (f", tensor parallel over {world} GPUs" if self.tp else ""))
 
     def prompt_ids(self) -> np.ndarray:
