@@ -118,3 +118,14 @@ def test_weight_bytes_formula():
     c = configs.LLAMA8B_Q4_0
     # 4.2214 GB of Q4_0 weights incl. the 0.2955 GB head (algorithmic bytes per token)
     assert abs(c.weight_bytes_per_token() / 1e9 - 4.2214) < 0.01
+
+
+def test_prefill_gemm_params_formula():
+    """Weights a prompt token multiplies in fwb_prefill's GEMMs: QKV in every
+    layer, o-proj and the FFN in all layers but the last."""
+    c = configs.LLAMA8B_Q4_0
+    E, F, hd = c.n_embd, c.n_ff, c.head_dim
+    q, kv = c.n_head * hd, c.n_head_kv * hd
+    want = 32 * (q + 2 * kv) * E + 31 * (q * E + 3 * E * F)
+    assert c.prefill_gemm_params() == want
+    assert abs(2 * want / 1e9 - 13.57) < 0.01  # GFLOP per prompt token
