@@ -320,7 +320,7 @@ __device__ void attn_phase(const Phase &P, uint8_t *scratch, uint32_t pos) {
 // the prologue / epilogue and the pairing only per-thread offsets, so a model
 // with one quant type runs one copy of the row loop for every GEMV phase
 // (instruction-cache footprint).
-template <int QT, bool A4>
+template <int QT, bool A4, bool HALF = false>
 __device__ __noinline__ PhaseResult gemv_phase_t(const GemvArgs *g, GemvSmem sm, RingState rs, const StageSrc *tab,
                                                  uint32_t n_ph, uint32_t total, uint32_t NS, uint32_t stage_bytes,
                                                  uint32_t pos) {
@@ -331,16 +331,16 @@ __device__ __noinline__ PhaseResult gemv_phase_t(const GemvArgs *g, GemvSmem sm,
         if (j + NS < total) issue_global(tab, n_ph, j + NS, ring, stage_bytes, full, slot, cursor);
     };
     PhaseResult r;
-    r.ok = gemv_consume<QT, A4>(*g, sm, threadIdx.x, rs, refill, pos);
+    r.ok = gemv_consume<QT, A4, decltype(refill), HALF>(*g, sm, threadIdx.x, rs, refill, pos);
     r.rs = rs;
     return r;
 }
 
-template <int QT>
+template <int QT, bool HALF = false>
 __device__ PhaseResult gemv_phase_q(const Phase &P, const GemvSmem &sm, const RingState &rs, const StageSrc *tab,
                                     uint32_t n_ph, uint32_t total, uint32_t NS, uint32_t stage_bytes, uint32_t pos) {
-    return P.a4 ? gemv_phase_t<QT, true>(&P.g, sm, rs, tab, n_ph, total, NS, stage_bytes, pos)
-                : gemv_phase_t<QT, false>(&P.g, sm, rs, tab, n_ph, total, NS, stage_bytes, pos);
+    return P.a4 ? gemv_phase_t<QT, true, HALF>(&P.g, sm, rs, tab, n_ph, total, NS, stage_bytes, pos)
+                : gemv_phase_t<QT, false, HALF>(&P.g, sm, rs, tab, n_ph, total, NS, stage_bytes, pos);
 }
 
 // The persistent kernel.  Q4A4 != 0: every GEMV phase is Q4_0 with 4-byte
@@ -348,8 +348,10 @@ __device__ PhaseResult gemv_phase_q(const Phase &P, const GemvSmem &sm, const Ri
 // AGQ.  Such a specialisation holds one copy of the row loop and one of the
 // attention instead of all of them: less code to fetch at every phase switch
 // (measured 4 % per decode step on the 8B model).  decode_kernel_t<0, 0, 0>
-// runs any model.
-template <int Q4A4, int AHD, int AGQ>
+// runs any model.  HALF: two GEMV rows per thread per round instead of four
+// (one instead of two for Q8_0), for models whose ring of four-row stages
+// does not fit next to the other shared memory (the 70B shapes).
+template <int Q4A4, int AHD, int AGQ, bool HALF = false>
 __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel_t(const __grid_constant__ DecodeArgs d) {
     extern __shared__ __align__(128) uint8_t smem[];
     const uint32_t tid = threadIdx.x;
@@ -413,12 +415,12 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel_t(const __gri
                 sm.red = reinterpret_cast<float *>(smem + kHeaderBytes + plane_bytes(P.g.K));
                 PhaseResult r{rs, false};
                 if constexpr (Q4A4 != 0) {
-                    r = gemv_phase_t<QT_Q4_0, true>(&P.g, sm, rs, tab, d.n_ph, total, d.NS, d.stage_bytes, pos);
+                    r = gemv_phase_t<QT_Q4_0, true, HALF>(&P.g, sm, rs, tab, d.n_ph, total, d.NS, d.stage_bytes, pos);
                 } else {
                     switch (P.qt) {
-                    case QT_Q4_0: r = gemv_phase_q<QT_Q4_0>(P, sm, rs, tab, d.n_ph, total, d.NS, d.stage_bytes, pos); break;
-                    case QT_Q5_0: r = gemv_phase_q<QT_Q5_0>(P, sm, rs, tab, d.n_ph, total, d.NS, d.stage_bytes, pos); break;
-                    case QT_Q8_0: r = gemv_phase_q<QT_Q8_0>(P, sm, rs, tab, d.n_ph, total, d.NS, d.stage_bytes, pos); break;
+                    case QT_Q4_0: r = gemv_phase_q<QT_Q4_0, HALF>(P, sm, rs, tab, d.n_ph, total, d.NS, d.stage_bytes, pos); break;
+                    case QT_Q5_0: r = gemv_phase_q<QT_Q5_0, HALF>(P, sm, rs, tab, d.n_ph, total, d.NS, d.stage_bytes, pos); break;
+                    case QT_Q8_0: r = gemv_phase_q<QT_Q8_0, HALF>(P, sm, rs, tab, d.n_ph, total, d.NS, d.stage_bytes, pos); break;
                     default: break;
                     }
                 }

@@ -54,7 +54,11 @@ template <> struct QTraits<QT_Q4_0> { static constexpr int BB = 18, OFF = 8, RPT
 template <> struct QTraits<QT_Q5_0> { static constexpr int BB = 22, OFF = 16, RPT = 4; };
 template <> struct QTraits<QT_Q8_0> { static constexpr int BB = 34, OFF = 0, RPT = 2; };
 
-__host__ __device__ constexpr uint32_t rows_per_thread(int qt) { return qt == QT_Q8_0 ? 2u : 4u; }
+// half: the halved row count (2, 1 for Q8_0) that the persistent kernel uses
+// when the ring of four-row stages does not fit its shared memory
+__host__ __device__ constexpr uint32_t rows_per_thread(int qt, bool half = false) {
+    return (qt == QT_Q8_0 ? 2u : 4u) >> (half ? 1 : 0);
+}
 
 enum GemvMode : int {
     GM_STORE = 0,   // y[r]  = (W x)[r]
@@ -517,7 +521,7 @@ __device__ __forceinline__ void rope_pair(float v0, float v1, float c, float s, 
 // row loop (no CTA-wide barrier: each warp reduces its partial sums of a batch
 // of 8 rows per slot with shuffles and parks them in shared memory), one CTA
 // barrier, then the epilogue over all local rows.
-template <int QT, bool A4, class Refill>
+template <int QT, bool A4, class Refill, bool HALF = false>
 __device__ bool gemv_consume(const GemvArgs &a, const GemvSmem &sm, uint32_t tid, RingState &rs,
                              const Refill &refill, uint32_t pos_known = kPosUnknown) {
     // run-time: the mode only changes the prologue / epilogue, pairing only the
@@ -526,7 +530,7 @@ __device__ bool gemv_consume(const GemvArgs &a, const GemvSmem &sm, uint32_t tid
     const bool PAIRED = MODE == GM_SWIGLU;
     constexpr int BB = QTraits<QT>::BB;
     constexpr int OFF = QTraits<QT>::OFF;
-    constexpr uint32_t RPT = QTraits<QT>::RPT;
+    constexpr uint32_t RPT = (uint32_t)QTraits<QT>::RPT >> (HALF ? 1 : 0);
     constexpr int RND = kRB / (int)RPT;  // rounds per reduction batch
     const uint32_t NC = blockDim.x, lane = tid & 31, warp = tid >> 5, NCW = NC >> 5;
     uint32_t rb, re;

@@ -121,7 +121,7 @@ constexpr uint32_t kRingBudget = 192 * 1024;
 constexpr uint32_t kMaxSmem = 227 * 1024;  // per-block opt-in limit (static + dynamic)
 
 // Fills geometry fields of L.a (w, n_out, K, row_bytes set by the caller).
-static bool plan_gemv(int qt, int mode, int sms, GemvLaunch &L) {
+static bool plan_gemv(int qt, int mode, int sms, GemvLaunch &L, bool half_rows = false) {
     GemvArgs &a = L.a;
     const uint32_t nb = a.K / 32;
     if (a.K % 32 || nb == 0 || a.n_out == 0) { set_err("gemv: bad shape"); return false; }
@@ -140,12 +140,12 @@ static bool plan_gemv(int qt, int mode, int sms, GemvLaunch &L) {
     const uint32_t grid = std::max(1u, std::min((uint32_t)sms, units));
     const uint32_t max_units = (units + grid - 1) / grid;
     const uint32_t max_loc = max_units * a.gran * (paired ? 2 : 1);
-    if ((paired || mode == GM_QKV) && (rows_per_thread(qt) * a.S) % 2) {  // whole pairs per stage
+    if ((paired || mode == GM_QKV) && (rows_per_thread(qt, half_rows) * a.S) % 2) {  // whole pairs per stage
         if (a.S == 1) { set_err("gemv: odd stage rows for a pair mode"); return false; }
         a.S &= ~1u;
         a.NC = a.S * a.Upad;
     }
-    const uint32_t R = rows_per_thread(qt) * a.S;  // rows per round = per ring stage
+    const uint32_t R = rows_per_thread(qt, half_rows) * a.S;  // rows per round = per ring stage
     a.R = R;
     uint32_t stage;
     if (paired) {
@@ -397,6 +397,7 @@ struct fwb_model {
     fwb::DecodeArgs dargs{};
     size_t dsmem = 0;
     const void *decode_fn = nullptr;  // the persistent kernel's specialisation for this model
+    bool half_rows = false;           // GEMV stages of two rows per thread (persistent ring too large otherwise)
     uint32_t *sync = nullptr;
     std::vector<void *> allocs;
     // tensor parallelism (world > 1): this rank's exchange buffer, every
@@ -722,6 +723,8 @@ static bool build_steps(fwb_model *m) {
     };
     auto part_out = [&]() { return reinterpret_cast<float *>(m->xbuf + m->x_part + (uint64_t)(n_ar & 1) * E * 4); };
     m->steps.clear();
+    if (const char *hr = getenv("FWB_HALF_ROWS"))  // (testing: the two-row stages on any model)
+        if (*hr == '1' && m->persistent) m->half_rows = true;
 
     {  // embedding
         Step s;
@@ -761,7 +764,7 @@ static bool build_steps(fwb_model *m) {
         L.a.y = y;
         L.a.step = m->step;
         L.a.err = m->err;
-        if (!plan_gemv((int)w.type, mode, m->sms, L)) return false;
+        if (!plan_gemv((int)w.type, mode, m->sms, L, m->half_rows)) return false;
         Step s;
         s.name = name;
         s.bytes = L.weight_bytes;
@@ -881,7 +884,15 @@ static bool build_steps(fwb_model *m) {
     // The head GEMV needs a norm weight; a model without output_norm gets the
     // identity norm (transformer.c:355-357 copies x unnormalised): not supported.
     if (!m->out_norm) { set_err("output_norm.weight is required by this build"); return false; }
-    return !m->persistent || build_decode(m);
+    if (!m->persistent) return true;
+    if (build_decode(m)) return true;
+    // a ring of four-row stages that does not fit next to the attention
+    // scratch and the stream tables (the 70B shapes): plan the GEMVs again
+    // with two rows per thread per round
+    if (m->half_rows || g_err.find("shared memory too small") == std::string::npos) return false;
+    m->half_rows = true;
+    g_err.clear();
+    return build_steps(m);
 }
 
 // Bytes of the attention scratch of the persistent kernel (16 warps).
@@ -932,11 +943,16 @@ static bool build_decode(fwb_model *m) {
         for (const Phase &p : ph)
             if (p.kind == PH_GEMV && (p.qt != QT_Q4_0 || !p.a4)) q4a4 = false;
         const uint32_t hd = m->cfg.head_dim, gq = m->cfg.n_head / m->cfg.n_head_kv;
-        m->decode_fn = (const void *)decode_kernel_t<0, 0, 0>;
-        if (q4a4 && hd == 128 && gq == 4) m->decode_fn = (const void *)decode_kernel_t<1, 128, 4>;
-        if (q4a4 && hd == 128 && gq == 8) m->decode_fn = (const void *)decode_kernel_t<1, 128, 8>;
         const char *gen = getenv("FWB_GENERIC_KERNEL");
-        if (gen && *gen == '1') m->decode_fn = (const void *)decode_kernel_t<0, 0, 0>;
+        const bool generic = gen && *gen == '1';
+        if (!m->half_rows) {
+            m->decode_fn = (const void *)decode_kernel_t<0, 0, 0, false>;
+            if (!generic && q4a4 && hd == 128 && gq == 4) m->decode_fn = (const void *)decode_kernel_t<1, 128, 4, false>;
+            if (!generic && q4a4 && hd == 128 && gq == 8) m->decode_fn = (const void *)decode_kernel_t<1, 128, 8, false>;
+        } else {
+            m->decode_fn = (const void *)decode_kernel_t<0, 0, 0, true>;
+            if (!generic && q4a4 && hd == 128 && gq == 8) m->decode_fn = (const void *)decode_kernel_t<1, 128, 8, true>;
+        }
     }
     cudaFuncAttributes fa;
     CK(cudaFuncGetAttributes(&fa, m->decode_fn));

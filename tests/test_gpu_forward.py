@@ -177,3 +177,22 @@ def test_long_context_more_than_32_splits_vs_oracle(gpu, model_dir):
         mism, wa, wr, gap = greedy_compare(m.forward, orc.forward, 5, pos0, 4)
     assert not mism, f"greedy mismatches: {mism}"
     assert wa <= 1e-2 and wr <= 1e-3
+
+
+@pytest.mark.parametrize("tag", ["mixed", "q4_0"])
+def test_half_row_stages_match_reference_golden(gpu, model_dir, monkeypatch, tag):
+    """The persistent kernel's two-rows-per-thread GEMV stages (used when the
+    four-row ring does not fit shared memory, as for the 70B shapes), forced
+    on a small model: the reference's golden logits and greedy tokens."""
+    monkeypatch.setenv("FWB_HALF_ROWS", "1")
+    g = np.load(os.path.join(GOLDEN, f"ref_decode_{tag}_plain.npz"))
+    cfg, seed = mg.GOLDEN_MODELS[tag]
+    path = _model_path(model_dir, cfg, seed, f"golden_{tag}")
+    pos0 = int(g["pos0"])
+    with Model(path) as m:
+        tok = int(g["first"])
+        for i, (ref_tok, ref_lg) in enumerate(zip(g["tokens"], g["logits"])):
+            lg = m.forward(tok, pos0 + i)
+            assert_logits_close(lg, ref_lg, f"step {i}")
+            assert int(np.argmax(lg)) == int(ref_tok), f"greedy token differs at step {i}"
+            tok = int(ref_tok)
