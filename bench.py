@@ -3,9 +3,11 @@
 
 Workload (N=1, benchmark configuration 3): the Llama-3-8B-shaped decoder with every linear weight in
 GGUF Q4_0 (embedding and norms fp32), random-init N(0, 0.02) from a seed and
-written as a GGUF file.  A 512-token uniform-random prompt is fed through the
-per-token forward (the reference's own prompt loop, main.c:145-151), then
-greedy decode runs at batch 1: W untimed warm-up tokens, then K timed tokens.
+written as a GGUF file.  A 512-token uniform-random prompt goes through
+fwb_prefill (all prompt tokens through each layer together on the tensor
+cores; the reference feeds a prompt one token at a time, main.c:145-151; the
+prompt is timed separately, the `prefill` key), then greedy decode runs at
+batch 1: W untimed warm-up tokens, then K timed tokens.
 One step = one token = one `transformer_forward` (one launch of the
 persistent decode kernel).
 
@@ -70,12 +72,15 @@ class Workload:
     decode stream for the whole box: strong scaling).
     """
 
-    def __init__(self, world: int):
+    def __init__(self, world: int, layers: int = 0):
         self.tp = world > 1
-        self.cfg = configs.LLAMA70B_Q4_0 if self.tp else configs.LLAMA8B_Q4_0
+        self.base = configs.LLAMA70B_Q4_0 if self.tp else configs.LLAMA8B_Q4_0
+        self.cfg = configs.with_layers(self.base, layers) if layers else self.base
         self.prompt = 256 if self.tp else 512
         shape = "Llama-70B" if self.tp else "Llama-3-8B"
         feed = "one decode step per token" if self.tp else "fwb_prefill"
+        if layers:
+            shape += f" (first {layers} layers only: a profiler case, not a bench value)"
         self.text = (f"{shape}-shaped decoder, all linear weights Q4_0, fp32 embedding/norms, "
                      f"random-init N(0,0.02); {self.prompt}-token random prompt ({feed}), then "
                      f"greedy decode at batch 1" + (f", tensor parallel over {world} GPUs" if self.tp else ""))
@@ -111,9 +116,11 @@ def _args():
                    help="skip the timed reference sample in the b200 arm")
     p.add_argument("--cpu-budget-s", type=float, default=15.0,
                    help="CPU seconds for the reference sample inside the b200 arm")
-    p.add_argument("--ref-budget-s", type=float, default=150.0,
+    p.add_argument("--ref-budget-s", type=float, default=300.0,
                    help="cap on the timed CPU seconds of the --impl reference arm")
     p.add_argument("--model-dir", default=None, help="where the synthetic GGUF is cached")
+    p.add_argument("--layers", type=int, default=0,
+                   help="profiler case: the same model with only its first N layers (not a bench value)")
     return p.parse_args()
 
 
@@ -133,7 +140,16 @@ def _dist():
 
 
 def _model_path(args, wl: Workload) -> str:
-    return gguf_synth.cached_model(wl.cfg, seed=MODEL_SEED, directory=args.model_dir)
+    """The cached synthetic GGUF, written (once) by a child process: neither
+    arm loads the generator library."""
+    return gguf_synth.cached_model_subprocess(wl.base.name, MODEL_SEED, args.model_dir, layers=args.layers)
+
+
+def _kv_ctx(wl: Workload, k_steps: int, w_steps: int) -> int:
+    """KV length both arms allocate: the prompt, the warm-up and the timed
+    decode steps of the b200 arm (which decodes twice: device-timed, then e2e)."""
+    need = wl.prompt + 2 * (w_steps + k_steps) + 1
+    return max(1024, 1 << (need - 1).bit_length())
 
 
 # ---------------------------------------------------------------------------
@@ -206,17 +222,17 @@ def _reference_model(path: str, kv_ctx: int):
     return pyoracle.OracleModel(path, max_ctx=kv_ctx), "port"
 
 
-def _time_reference(path: str, wl: Workload, n_max: int, budget_s: float, warm: int = 1):
-    """Decode steps of the reference at positions prompt.. after a K/V pre-fill.
-
-    The prompt's K/V rows are written directly (N(0,1) values) instead of
-    running the prompt on the CPU (about an hour for the 8B model); each timed
-    step then does the same weight streaming and the same attention length as
-    a real decode step.  Returns (tokens/s, steps timed, kind, seconds).
-    """
+def _time_reference(path: str, wl: Workload, kv_ctx: int, warm: int, n_max: int, budget_s: float):
+    """Decode steps of the reference on the host, at the positions the b200
+    arm decodes: a K/V pre-fill of the prompt's positions [0, P), `warm`
+    untimed steps at P.., then up to n_max timed steps (fewer if budget_s runs
+    out).  The prompt's K/V rows are written directly (N(0,1) values) instead
+    of running the prompt on the CPU (about an hour for the 8B model); each
+    timed step then does the same weight streaming and the same attention
+    length as the b200 arm's step at that position.
+    Returns (tokens/s, steps timed, kind, seconds, first timed position)."""
     c, P = wl.cfg, wl.prompt
-    n_max = max(1, min(n_max, 512))
-    ref, kind = _reference_model(path, P + warm + n_max + 1)
+    ref, kind = _reference_model(path, kv_ctx)
     rng = np.random.default_rng(7)
     for layer in range(c.n_layer):
         k = rng.standard_normal((P, c.n_head_kv, c.head_dim), dtype=np.float32)
@@ -226,7 +242,7 @@ def _time_reference(path: str, wl: Workload, n_max: int, budget_s: float, warm: 
     for _ in range(warm):
         tok = int(np.argmax(ref.forward(tok, pos)))
         pos += 1
-    n, t0 = 0, time.perf_counter()
+    first, n, t0 = pos, 0, time.perf_counter()
     while n < n_max:
         tok = int(np.argmax(ref.forward(tok, pos)))
         pos += 1
@@ -235,26 +251,29 @@ def _time_reference(path: str, wl: Workload, n_max: int, budget_s: float, warm: 
             break
     dt = time.perf_counter() - t0
     ref.close()
-    return n / dt, n, kind, dt
+    return n / dt, n, kind, dt, first
 
 
 def run_reference(args) -> None:
+    """The reference's own CPU decode step on the b200 arm's workload: same
+    model file, same K/V length, same warm-up count and decode positions."""
     rank, world, _ = _dist()
     if rank != 0:
         return
-    wl = Workload(args.gpus)
+    wl = Workload(args.gpus, args.layers)
     path = _model_path(args, wl)
-    tps, n, kind, dt = _time_reference(path, wl, args.steps, args.ref_budget_s, warm=1)
-    P = wl.prompt
-    sample = (f"{n} greedy decode steps of the {wl.cfg.name} model at positions {P + 1}..{P + n} after a "
-              f"{P}-position K/V pre-fill (1 untimed warm-up step; {args.steps} requested, capped at "
-              f"{args.ref_budget_s:.0f} s)")
+    K, W = args.steps, args.warmup
+    kv_ctx = _kv_ctx(wl, K, W)
+    tps, n, kind, dt, first = _time_reference(path, wl, kv_ctx, W, K, args.ref_budget_s)
+    sample = (f"{n} greedy decode steps of the {wl.cfg.name} model at positions {first}..{first + n - 1} "
+              f"after a {wl.prompt}-position K/V pre-fill and {W} untimed warm-up steps"
+              + ("" if n == K else f" ({K} requested, cut at the {args.ref_budget_s:.0f} s cap)"))
     line = {
         "metric": METRIC, "value": tps, "unit": UNIT, "n_gpus": args.gpus, "steps": n,
-        "warmup": 1, "ms_per_step": dt / n * 1e3, "higher_is_better": True,
+        "warmup": W, "ms_per_step": dt / n * 1e3, "higher_is_better": True,
         "scaling": "strong" if wl.tp else "weak",
         "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded random weights and prompt)",
-        "config": wl.config(args.gpus, n, 1, P + n + 2), "impl": "reference",
+        "config": wl.config(args.gpus, K, W, kv_ctx), "impl": "reference",
         "cpu_baseline": {"value": tps, "unit": UNIT, "cores": 1, "kind": kind, "sample": sample,
                          "host_cores": os.cpu_count(),
                          "note": "the reference decode step is single-threaded by design"},
@@ -276,7 +295,7 @@ def run_b200(args) -> None:
     rank, world, local = _dist()
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
-    wl = Workload(world)
+    wl = Workload(world, args.layers)
     torch.cuda.set_device(local)
     if world > 1:
         # host coordination only (IPC handles, barriers, the max over ranks):
@@ -304,10 +323,9 @@ def run_b200(args) -> None:
     if K < 1 or W < 0:
         raise SystemExit("--steps must be >= 1 and --warmup >= 0")
     P = wl.prompt
-    need = P + 2 * (W + K) + 1
-    kv_ctx = max(1024, 1 << (need - 1).bit_length())
+    kv_ctx = _kv_ctx(wl, K, W)
     if kv_ctx > wl.cfg.n_ctx:
-        raise SystemExit(f"--steps/--warmup need {need} positions > n_ctx {wl.cfg.n_ctx}")
+        raise SystemExit(f"--steps/--warmup need more than n_ctx {wl.cfg.n_ctx} positions")
 
     m = tp.open_model(path, kv_ctx, rank, world, local) if world > 1 else Model(path, max_ctx=kv_ctx, device=local)
     stream = torch.cuda.ExternalStream(m.stream, device=torch.device(f"cuda:{local}"))
@@ -408,7 +426,8 @@ def run_b200(args) -> None:
             "roofline": {
                 "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "peak_source": f"hbm_gbs ({peak_kind})",
-                "traffic": None if wl.tp else _ncu_traffic(),
+                "traffic": None if wl.tp or args.layers else _ncu_traffic()[0],
+                "traffic_source": None if wl.tp or args.layers else _ncu_traffic()[1],
                 "kernel": "decode_kernel (persistent, one launch per token" +
                           (", per GPU)" if wl.tp else ")"),
                 "bytes_per_launch": step_bytes,
@@ -428,27 +447,35 @@ def run_b200(args) -> None:
             line["roofline"]["note"] = ("per GPU: its weight slices; the box-wide tokens/s is the value "
                                         "(one decode stream across all GPUs)")
         if world == 1 and not args.no_cpu_baseline:
-            tps, n, kind, dt = _time_reference(path, wl, 1 << 30, args.cpu_budget_s, warm=1)
+            tps, n, kind, dt, first = _time_reference(path, wl, kv_ctx, 1, 1 << 30, args.cpu_budget_s)
             line["cpu_baseline"] = {
                 "value": tps, "unit": UNIT, "cores": 1, "kind": kind, "host_cores": os.cpu_count(),
                 "sample": f"{n} greedy decode steps of the same model at positions "
-                          f"{P + 1}..{P + n} after a {P}-position K/V pre-fill ({dt:.1f} s)"}
+                          f"{first}..{first + n - 1} after a {P}-position K/V pre-fill and 1 "
+                          f"warm-up step ({dt:.1f} s)"}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
 
 
 def _ncu_traffic():
-    """DRAM bytes per decode-kernel launch from the committed ncu summary, if any."""
+    """DRAM bytes per decode-kernel launch, read from the committed ncu summary
+    (not measured in this run: ncu cannot run inside the timed bench), with
+    the summary's statement of which kernel source it was captured on."""
     p = os.path.join(ROOT, "profiles", "decode_kernel_8b_q4_0.md")
+    val, src = None, None
     try:
         with open(p) as f:
             for line in f:
                 if line.startswith("traffic_bytes_per_launch:"):
-                    return float(line.split(":", 1)[1])
+                    val = float(line.split(":", 1)[1])
+                if line.startswith("kernel_source:"):
+                    src = line.split(":", 1)[1].strip()
     except OSError:
         pass
-    return None
+    if val is None:
+        return None, None
+    return val, f"from profiles/decode_kernel_8b_q4_0.md (ncu capture; {src or 'kernel source not stated'})"
 
 
 def main() -> None:

@@ -756,6 +756,10 @@ __device__ bool gemv_consume(const GemvArgs &a, const GemvSmem &sm, uint32_t tid
                 bi = sm.misc_u[0];
                 for (uint32_t w = 1; w < NCW; ++w)
                     if (sm.misc[w] > bv || (sm.misc[w] == bv && sm.misc_u[w] < bi)) { bv = sm.misc[w]; bi = sm.misc_u[w]; }
+                // sampler_argmax (sampler.c:28-32) starts from index 0 and
+                // moves only on a strict '>': a NaN logit 0 is never beaten,
+                // so the token is 0 (as +inf at index 0 for the ranks' merge)
+                if (a.idx_base == 0 && isnan(__ldcg(&a.y[0]))) { bv = INFINITY; bi = 0; }
                 if (a.tp_cand) {  // the ranks' candidates are combined after a global barrier
                     a.tp_cand[0] = bv;
                     reinterpret_cast<uint32_t *>(a.tp_cand)[1] = bi;

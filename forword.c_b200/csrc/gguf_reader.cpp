@@ -146,13 +146,14 @@ bool GgufFile::open(const std::string &path, std::string &err) {
             c2.take(4);
             n_tokens_ = c2.take(8);
         }
+        skip_value(c, kv.type, 0);
+        if (c.bad) { err = "malformed metadata entry"; return false; }
+        // (read only after skip_value has checked that the value lies inside the file)
         if (kv.key == "general.alignment" && (kv.type == 4 || kv.type == 5)) {
             uint32_t a;
             std::memcpy(&a, kv.val, 4);
             if (a > 0 && a <= 4096 && (a & (a - 1)) == 0) alignment_ = a;
         }
-        skip_value(c, kv.type, 0);
-        if (c.bad) { err = "malformed metadata entry"; return false; }
         kvs_.push_back(std::move(kv));
     }
     tensors_.resize(n_t);

@@ -239,12 +239,25 @@ static bool matvec_args_ok(const void *w, size_t w_size, uint32_t type, const vo
     return true;
 }
 
+// Bytes from w to the 16-byte boundary at or after the end of `rows` bytes
+// of rows: the GEMV's bulk copies move 16-byte aligned supersets of the
+// rows, so that span must lie inside the caller's buffer.
+static uint64_t span16(const void *w, uint64_t rows) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(w);
+    return ((a + rows + 15) & ~uintptr_t(15)) - a;
+}
+
 static bool matvec_dev(const void *w, size_t w_size, uint32_t type, const float *x, float *y, size_t in, size_t out,
                        cudaStream_t st) {
     uint32_t bb, row_bytes;
     if (!matvec_args_ok(w, w_size, type, x, y, in, out, bb, row_bytes)) return false;
     if ((uintptr_t)w % 2) { set_err("quant_matvec_dev: weights must be 2-byte aligned"); return false; }
     if ((uintptr_t)x % 16) { set_err("quant_matvec_dev: input must be 16-byte aligned"); return false; }
+    if (span16(w, (uint64_t)out * row_bytes) > w_size) {
+        set_err("quant_matvec_dev: weights_size must reach the 16-byte boundary after the last row (" +
+                std::to_string(span16(w, (uint64_t)out * row_bytes)) + " bytes from d_weights)");
+        return false;
+    }
     int dev;
     CK(cudaGetDevice(&dev));
     if (!set_smem_attrs(dev)) return false;
@@ -258,8 +271,28 @@ static bool matvec_dev(const void *w, size_t w_size, uint32_t type, const float 
     L.a.err = device_err_word(dev);
     if (!L.a.err) { set_err("quant_matvec: device error word allocation failed"); return false; }
     if (!plan_gemv((int)type, GM_STORE, num_sms(dev), L)) return false;
+    CK(cudaMemsetAsync(L.a.err, 0, 4, st));  // status of this launch only
     void *args[] = {&L.a};
     CK(launch_ex(L.fn, L.grid, L.block, L.smem, st, args, false));
+    return true;
+}
+
+// The device error word of the current device after the work queued on `st`
+// (quant_matvec_dev / quant_gemm_dev): 0 when no bounded wait ran out.
+static bool device_status(cudaStream_t st, const char *who) {
+    int dev;
+    CK(cudaGetDevice(&dev));
+    uint32_t *w = device_err_word(dev);
+    if (!w) { set_err(std::string(who) + ": device error word allocation failed"); return false; }
+    uint32_t e = 0;
+    CK(cudaMemcpyAsync(&e, w, 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    if (e) {
+        char b[96];
+        snprintf(b, sizeof b, "%s: device error word 0x%x (a bounded wait in the kernel ran out)", who, e);
+        set_err(b);
+        return false;
+    }
     return true;
 }
 
@@ -359,6 +392,10 @@ struct LayerW {
     Mat qkv, o, gate, up, down;
     const float *attn_norm = nullptr, *ffn_norm = nullptr;
 };
+
+// m->step words: [0] token, [1] position, [2] greedy token out, [kErrWord]
+// the device error word
+constexpr uint32_t kErrWord = 8;
 
 struct Step {
     std::string name;
@@ -666,12 +703,16 @@ static bool load_model(fwb_model *m, const char *path, size_t max_ctx) {
         !dalloc(m, (void **)&m->vc, kvn * 4) ||
         !dalloc(m, (void **)&m->rope_cos, (size_t)m->kv_ctx * (hd / 2) * 4 + 4) ||
         !dalloc(m, (void **)&m->rope_sin, (size_t)m->kv_ctx * (hd / 2) * 4 + 4) ||
-        !dalloc(m, (void **)&m->step, 64) || !dalloc(m, (void **)&m->err, 16) ||
+        !dalloc(m, (void **)&m->step, 64) ||
         !dalloc(m, (void **)&m->hist, (size_t)m->kv_ctx * 4 + 4) ||
         !dalloc(m, (void **)&m->am_val, 4096 * 4) || !dalloc(m, (void **)&m->am_idx, 4096 * 4) ||
         !dalloc(m, (void **)&m->am_ticket, 64) || !dalloc(m, (void **)&m->attn_ticket, 4 * KVr + 64))
         return false;
+    // the device error word shares the step's allocation: set_step clears it
+    // with the same copy that sets the token and position
+    m->err = m->step + kErrWord;
     CK(cudaMallocHost(&m->h_io, 64));
+    std::memset(m->h_io, 0, 64);
     CK(cudaMallocHost(&m->h_logits, (size_t)c.n_vocab * 4));
 
     // RoPE tables exactly as rope_precompute (rope.c:6-17), on the host
@@ -765,6 +806,7 @@ static bool build_steps(fwb_model *m) {
         L.a.step = m->step;
         L.a.err = m->err;
         if (!plan_gemv((int)w.type, mode, m->sms, L, m->half_rows)) return false;
+        if (!norm_w) L.a.norm = 0u;  // LM head of a model without output_norm
         Step s;
         s.name = name;
         s.bytes = L.weight_bytes;
@@ -881,9 +923,9 @@ static bool build_steps(fwb_model *m) {
         s.run = [](cudaStream_t, bool) { return cudaErrorNotSupported; };
         m->steps.push_back(std::move(s));
     }
-    // The head GEMV needs a norm weight; a model without output_norm gets the
-    // identity norm (transformer.c:355-357 copies x unnormalised): not supported.
-    if (!m->out_norm) { set_err("output_norm.weight is required by this build"); return false; }
+    // (a model without output_norm feeds x to the head unnormalised, as
+    // transformer.c:304-306 copies it: the head GEMV then runs without the
+    // RMSNorm prologue)
     if (!m->persistent) return true;
     if (build_decode(m)) return true;
     // a ring of four-row stages that does not fit next to the attention
@@ -1112,13 +1154,19 @@ static bool finish(fwb_model *m) {
     return true;
 }
 
+// Token and position of the next step.  On one GPU the same copy zeroes
+// the device error word (step[kErrWord]), so each call reports only its own
+// launches; under tensor parallelism the word stays set once a wait ran out
+// (the ranks' cross-rank barrier counts no longer agree: reopen the model).
 static bool set_step(fwb_model *m, uint32_t tok, size_t pos) {
     if (m->world > 1 && !m->connected) { set_err("tensor parallel model: call fwb_tp_connect first"); return false; }
     if (pos >= m->kv_ctx) { set_err("transformer_forward: position exceeds KV cache"); return false; }
     if (tok >= m->cfg.n_vocab) { set_err("transformer_forward: token ID out of range"); return false; }
+    for (uint32_t i = 2; i <= kErrWord; ++i) m->h_io[i] = 0;
     m->h_io[0] = tok;
     m->h_io[1] = (uint32_t)pos;
-    CK(cudaMemcpyAsync(m->step, m->h_io, 8, cudaMemcpyHostToDevice, m->st));
+    const size_t n = m->world > 1 ? 8 : 4 * (kErrWord + 1);
+    CK(cudaMemcpyAsync(m->step, m->h_io, n, cudaMemcpyHostToDevice, m->st));
     return true;
 }
 
@@ -1152,8 +1200,9 @@ int quant_matvec(const void *weights, size_t weights_size, uint32_t ggml_type, c
         cudaMalloc(&dy, output_size * 4) == cudaSuccess &&
         cudaMemcpy(dw, weights, wbytes, cudaMemcpyHostToDevice) == cudaSuccess &&
         cudaMemcpy(dx, input, input_size * 4, cudaMemcpyHostToDevice) == cudaSuccess) {
-        if (matvec_dev(dw, wbytes, ggml_type, dx, dy, input_size, output_size, nullptr) &&
-            cudaMemcpy(output, dy, output_size * 4, cudaMemcpyDeviceToHost) == cudaSuccess)
+        if (matvec_dev(dw, wbytes + 64, ggml_type, dx, dy, input_size, output_size, nullptr) &&
+            cudaMemcpy(output, dy, output_size * 4, cudaMemcpyDeviceToHost) == cudaSuccess &&
+            device_status(nullptr, "quant_matvec"))
             rc = 0;
         else if (g_err.empty())
             set_err("quant_matvec: device execution failed");
@@ -1179,11 +1228,15 @@ int quant_matvec_dev(const void *d_weights, size_t weights_size, uint32_t ggml_t
                : -1;
 }
 
+int quant_device_status(void *stream) {
+    return device_status(static_cast<cudaStream_t>(stream), "quant_device_status") ? 0 : -1;
+}
+
 // Tensor-core dequant-GEMM launch (gemm_tc.cuh): Y[m][0..N) (row stride ldy)
 // = W X[m] for m < M, or += with TC_ADD.  Q4_0 with K a multiple of 64,
 // 4-byte-aligned weights and 16-byte-aligned fp16 activations only.
 static bool launch_tc_gemm(const void *w, size_t w_bytes, uint32_t type, const void *x, float *y, size_t K, size_t N,
-                           size_t M, size_t ldy, uint32_t mode, cudaStream_t st) {
+                           size_t M, size_t ldy, uint32_t mode, cudaStream_t st, uint32_t *err) {
     static bool attr_set[64] = {};
     if (!w || !x || !y || !K || !N || !M) { set_err("quant_gemm: null pointer or zero size"); return false; }
     if (type != 2) { set_err("quant_gemm: only Q4_0 (type 2) runs on the tensor cores"); return false; }
@@ -1209,8 +1262,7 @@ static bool launch_tc_gemm(const void *w, size_t w_bytes, uint32_t type, const v
     a.K = (uint32_t)K;
     a.ldy = (uint32_t)ldy;
     a.mode = mode;
-    a.err = device_err_word(dev);
-    if (!a.err) { set_err("quant_gemm: device error word"); return false; }
+    a.err = err;
     const dim3 grid((unsigned)((N + kTcN - 1) / kTcN), (unsigned)((M + kTcM - 1) / kTcM));
     gemm_q4_0_tc_kernel<<<grid, kTcThreads, kTcSmem, st>>>(a);
     cudaError_t e = cudaGetLastError();
@@ -1221,8 +1273,16 @@ static bool launch_tc_gemm(const void *w, size_t w_bytes, uint32_t type, const v
 int quant_gemm_dev(const void *d_weights, size_t weights_size, uint32_t ggml_type, const void *d_input_f16,
                    float *d_output, size_t input_size, size_t output_size, size_t n_tokens, int accumulate,
                    void *stream) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) { set_err("quant_gemm_dev: no device"); return -1; }
+    uint32_t *err = device_err_word(dev);
+    if (!err) { set_err("quant_gemm_dev: device error word"); return -1; }
+    if (cudaMemsetAsync(err, 0, 4, static_cast<cudaStream_t>(stream)) != cudaSuccess) {  // this launch only
+        set_err("quant_gemm_dev: error word reset failed");
+        return -1;
+    }
     if (!launch_tc_gemm(d_weights, weights_size, ggml_type, d_input_f16, d_output, input_size, output_size, n_tokens,
-                        output_size, accumulate ? TC_ADD : TC_STORE, static_cast<cudaStream_t>(stream)))
+                        output_size, accumulate ? TC_ADD : TC_STORE, static_cast<cudaStream_t>(stream), err))
         return -1;
     return 0;
 }
@@ -1441,24 +1501,25 @@ static bool prefill_chunk(fwb_model *m, const uint32_t *tokens, uint32_t T, uint
         float *kc = m->kc + l * layer_kv, *vc = m->vc + l * layer_kv;
         pf_rmsnorm_f16_kernel<<<T, 256, 0, st>>>(m->pf_x, w.attn_norm, c.norm_eps, E, m->pf_h16);
         if (!launch_tc_gemm(w.qkv.p, (size_t)w.qkv.rows * w.qkv.row_bytes, 2, m->pf_h16, m->pf_qkv, E, NQKV, T, NQKV,
-                            TC_STORE, st))
+                            TC_STORE, st, m->err))
             return false;
         pf_rope_kv_kernel<<<T, 256, 0, st>>>(m->pf_qkv, p0, NQ, NKV, hd, m->rope_cos, m->rope_sin, m->pf_q, kc, vc,
                                              m->kv_ctx);
         if (!launch_pf_attn(m, kc, vc, T, p0, att_smem, st)) return false;
         if (l + 1 == c.n_layer) break;  // the last layer's output feeds only the logits
-        if (!launch_tc_gemm(w.o.p, (size_t)w.o.rows * w.o.row_bytes, 2, m->pf_a16, m->pf_x, NQ, E, T, E, TC_ADD, st))
+        if (!launch_tc_gemm(w.o.p, (size_t)w.o.rows * w.o.row_bytes, 2, m->pf_a16, m->pf_x, NQ, E, T, E, TC_ADD, st,
+                            m->err))
             return false;
         pf_rmsnorm_f16_kernel<<<T, 256, 0, st>>>(m->pf_x, w.ffn_norm, c.norm_eps, E, m->pf_h16);
         if (!launch_tc_gemm(w.gate.p, (size_t)w.gate.rows * w.gate.row_bytes, 2, m->pf_h16, m->pf_g, E, F, T, F,
-                            TC_STORE, st) ||
+                            TC_STORE, st, m->err) ||
             !launch_tc_gemm(w.up.p, (size_t)w.up.rows * w.up.row_bytes, 2, m->pf_h16, m->pf_u, E, F, T, F, TC_STORE,
-                            st))
+                            st, m->err))
             return false;
         pf_swiglu_kernel<<<std::min<size_t>(4096, ((size_t)T * F + 255) / 256), 256, 0, st>>>(
             m->pf_g, m->pf_u, (size_t)T * F, m->pf_h16);
         if (!launch_tc_gemm(w.down.p, (size_t)w.down.rows * w.down.row_bytes, 2, m->pf_h16, m->pf_x, F, E, T, E,
-                            TC_ADD, st))
+                            TC_ADD, st, m->err))
             return false;
     }
     cudaError_t e = cudaGetLastError();
@@ -1481,10 +1542,12 @@ int fwb_prefill(fwb_model_t *m, const uint32_t *tokens, size_t n, size_t pos0, f
             if (fwb_forward(m, tokens[i], pos0 + i, nullptr) != 0) return -1;
     } else {
         if (!prefill_alloc(m)) return -1;
+        if (cudaMemsetAsync(m->err, 0, 4, m->st) != cudaSuccess) { set_err("prefill: error word reset"); return -1; }
         for (size_t i = 0; i + 1 < n; i += kPrefillChunk) {
             const uint32_t T = (uint32_t)std::min<size_t>(kPrefillChunk, n - 1 - i);
             if (!prefill_chunk(m, tokens + i, T, (uint32_t)(pos0 + i))) return -1;
         }
+        if (!finish(m)) return -1;  // a GEMM's bounded wait that ran out
     }
     // the last token through the decode step gives the logits
     return fwb_forward(m, tokens[n - 1], pos0 + n - 1, logits_host);
@@ -1619,10 +1682,24 @@ int fwb_trace_attn_read(fwb_model_t *m, uint64_t *out, size_t n) {
     if (n < cnt) { set_err("trace buffer too small"); return -1; }
     cudaSetDevice(m->dev);
     if (cudaMemcpy(out, m->attn_trace, cnt * 8, cudaMemcpyDeviceToHost) != cudaSuccess) { set_err("trace copy"); return -1; }
-    CK(cudaMemset(m->attn_trace, 0, cnt * 8));  // CTAs without an item in the next step stay 0
+    // CTAs without an item in the next step stay 0
+    if (cudaMemset(m->attn_trace, 0, cnt * 8) != cudaSuccess) { set_err("trace reset failed"); return -1; }
     return (int)cnt;
 }
 
 void *fwb_stream(fwb_model_t *m) { return m ? (void *)m->st : nullptr; }
+
+void *fwb_host_alloc(size_t bytes) {
+    void *p = nullptr;
+    if (!bytes || cudaMallocHost(&p, bytes) != cudaSuccess) {
+        set_err("fwb_host_alloc: page-locked allocation failed");
+        return nullptr;
+    }
+    return p;
+}
+
+void fwb_host_free(void *p) {
+    if (p) cudaFreeHost(p);
+}
 
 }  // extern "C"

@@ -26,6 +26,7 @@ class ModelShape:
     rope_base: float = 10000.0
     eps: float = 1e-5
     tied: bool = False
+    out_norm: bool = True   # False: no output_norm.weight (the head reads x unnormalised)
     # ggml type per tensor role
     t_embd: int = F32
     t_q: int = Q4_0
@@ -101,10 +102,19 @@ SMALL_Q4_0 = ModelShape("small-q4_0", n_embd=512, n_layer=2, n_head=4, n_head_kv
 SMALL_MIXED = replace(SMALL_Q4_0, name="small-mixed", t_q=Q8_0, t_k=Q8_0, t_v=Q8_0, t_o=Q8_0,
                       t_gate=Q5_0, t_up=Q5_0, t_down=Q8_0, t_out=Q8_0)
 SMALL_TIED_Q8 = replace(TINY, name="small-tied-q8_0", n_layer=2, n_vocab=1000, n_ctx=128)
+SMALL_NO_OUT_NORM = replace(SMALL_Q4_0, name="small-q4_0-no-out-norm", out_norm=False)
 # splits over 2, 4 or 8 tensor-parallel ranks (8 KV heads, 256 FFN rows and
 # 256 vocabulary rows per rank at 8 ranks)
 SMALL_TP8 = ModelShape("small-tp8", n_embd=1024, n_layer=2, n_head=8, n_head_kv=8, n_ff=2048,
                        n_vocab=2048, n_ctx=512, rope_base=500000.0)
 
 CONFIGS = {c.name: c for c in (TINY, LLAMA8B_Q4_0, LLAMA8B_MIXED, LLAMA70B_Q4_0, SMALL_TP8,
-                               SMALL_Q4_0, SMALL_MIXED, SMALL_TIED_Q8)}
+                               SMALL_Q4_0, SMALL_MIXED, SMALL_TIED_Q8, SMALL_NO_OUT_NORM)}
+
+
+def with_layers(cfg: ModelShape, n_layer: int) -> ModelShape:
+    """cfg with only its first n_layer layers (same shapes per layer): a
+    small case of the same kernels for profiler captures and parity slices."""
+    if n_layer == cfg.n_layer:
+        return cfg
+    return replace(cfg, name=f"{cfg.name}-{n_layer}layer", n_layer=n_layer)

@@ -79,7 +79,8 @@ def tensor_plan(cfg: ModelShape) -> list[tuple[str, int, int, int, str]]:
             (p + "ffn_up.weight", cfg.t_up, F, E, "w"),
             (p + "ffn_down.weight", cfg.t_down, E, F, "w"),
         ]
-    plan.append(("output_norm.weight", F32, 1, E, "norm"))
+    if cfg.out_norm:
+        plan.append(("output_norm.weight", F32, 1, E, "norm"))
     if not cfg.tied:
         plan.append(("output.weight", cfg.t_out, cfg.n_vocab, E, "w"))
     return plan
@@ -186,3 +187,39 @@ def normal_vector(n: int, seed: int, mean: float = 0.0, sd: float = 1.0) -> np.n
     lib.fwb_synth_normal(ctypes.c_void_p(out.ctypes.data), n, tensor_key(seed, "vector"),
                          mean, sd)
     return out
+
+
+def main(argv: list[str] | None = None) -> None:
+    """python -m fwb.gguf_synth CONFIG SEED [DIR]: write (once) the cached
+    synthetic model and print its path.  Run as its own process so that a
+    caller timing the reference never loads the generator library."""
+    import argparse
+    from .configs import CONFIGS, with_layers
+    p = argparse.ArgumentParser(description=main.__doc__.split("\n")[0])
+    p.add_argument("config")
+    p.add_argument("seed", type=int)
+    p.add_argument("directory", nargs="?", default=None)
+    p.add_argument("--layers", type=int, default=0, help="keep only the first N layers (0: all)")
+    a = p.parse_args(argv)
+    cfg = CONFIGS[a.config]
+    if a.layers:
+        cfg = with_layers(cfg, a.layers)
+    print(cached_model(cfg, seed=a.seed, directory=a.directory))
+
+
+def cached_model_subprocess(cfg_name: str, seed: int, directory: str | None = None, layers: int = 0) -> str:
+    """cached_model in a child process (see main); returns the path."""
+    import subprocess
+    import sys
+    pkg = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    cmd = [sys.executable, "-m", "fwb.gguf_synth", cfg_name, str(seed)]
+    if directory:
+        cmd.append(directory)
+    if layers:
+        cmd += ["--layers", str(layers)]
+    out = subprocess.run(cmd, check=True, capture_output=True, text=True, cwd=pkg)
+    return out.stdout.strip().splitlines()[-1]
+
+
+if __name__ == "__main__":
+    main()

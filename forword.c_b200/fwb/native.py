@@ -68,6 +68,10 @@ def _declare(lib) -> None:
     sig("quant_matvec_dev", _i32, _vp, _sz, _u32, _vp, _vp, _sz, _sz, _vp)
     sig("quant_gemm_dev", _i32, _vp, _sz, _u32, _vp, _vp, _sz, _sz, _sz, _i32, _vp)
     sig("quant_dequant_dev", _i32, _vp, _sz, _u32, _vp, _sz, _vp)
+    sig("quant_device_status", _i32, _vp)
+    sig("quant_matvec_static", _i32, _vp, _sz, _u32, _fp, _fp, _sz, _sz)
+    sig("fwb_host_alloc", _vp, _sz)
+    sig("fwb_host_free", None, _vp)
     sig("fwb_model_open", _vp, _c.c_char_p, _sz, _i32)
     sig("fwb_model_close", None, _vp)
     sig("fwb_model_dims", _i32, _vp, _c.POINTER(_u32))

@@ -69,7 +69,9 @@ int transformer_init(transformer_t *t, const char *path, size_t max_ctx) {
         goto fail;
     }
     t->n_ctx = d[1];
-    t->logits = malloc((size_t)c->n_vocab * sizeof(float));
+    /* page-locked (library-side cudaMallocHost): the logits row then comes
+     * back with one device-to-host copy and no staging memcpy */
+    t->logits = fwb_host_alloc((size_t)c->n_vocab * sizeof(float));
     if (!t->logits) {
         fprintf(stderr, "transformer_init: working buffer allocation failed\n");
         goto fail;
@@ -84,7 +86,7 @@ fail:
 void transformer_free(transformer_t *t) {
     if (!t) return;
     fwb_model_close(t->dev);
-    free(t->logits);
+    fwb_host_free(t->logits);
     tokenizer_free(t->tok);
     if (t->g.mapping) gguf_close(&t->g);  /* a zeroed struct holds no file (fd 0 is not ours) */
     memset(t, 0, sizeof(*t));

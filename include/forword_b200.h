@@ -90,15 +90,30 @@ int quant_matvec_static(const void *weights, size_t weights_size, uint32_t ggml_
 
 /*
  * Device-pointer form of quant_matvec for callers whose data already lives
- * in HBM.  d_weights must lie inside a cudaMalloc allocation and be 2-byte
- * aligned (the kernel reads up to 15 bytes either side of the rows, rounding
- * to 16-byte copies); d_input / d_output are fp32 device arrays.  `stream`
- * is a cudaStream_t (NULL = legacy default stream).  Asynchronous: returns
- * after enqueueing.
+ * in HBM; no reference counterpart (quant_matvec.h:7-15 is host-only).
+ * d_weights must be 2-byte aligned.  The kernel copies 16-byte aligned
+ * supersets of the rows: it reads from d_weights rounded down to 16 bytes
+ * (inside the same allocation unless d_weights is 16-byte aligned, as
+ * cudaMalloc pointers are) up to the 16-byte boundary at or after the last
+ * row, and weights_size must reach that boundary (-1 otherwise).  d_input /
+ * d_output are fp32 device arrays (d_input 16-byte aligned).  `stream` is a
+ * cudaStream_t (NULL = legacy default stream).  Asynchronous: returns after
+ * enqueueing; quant_device_status reports a kernel-side failure.
  */
 int quant_matvec_dev(const void *d_weights, size_t weights_size, uint32_t ggml_type,
                      const float *d_input, float *d_output, size_t input_size,
                      size_t output_size, void *stream);
+
+/*
+ * Status of the last quant_matvec_dev / quant_gemm_dev launch on the current
+ * device after the work queued on `stream` (synchronises it): 0 if the
+ * kernel completed, -1 (fwb_last_error() names the device error word) if one
+ * of its bounded waits ran out and part of the output was not written.  Each
+ * launch clears the word on its own stream first, so launches overlapping on
+ * different streams of one device share it.  No reference counterpart: the
+ * reference's quant_matvec is synchronous CPU code.
+ */
+int quant_device_status(void *stream);
 
 /*
  * Batched (prompt) form of quant_matvec_dev on the tensor cores:
@@ -153,7 +168,9 @@ int fwb_model_kernels_per_step(const fwb_model_t *m);
  * transformer_forward (transformer.c:149-326): feed token_id at position pos
  * and write n_vocab fp32 logits to logits_host (host memory; may be NULL to
  * skip the copy).  Errors as the reference: pos >= kv_ctx or
- * token_id >= n_vocab -> -1.
+ * token_id >= n_vocab -> -1.  A bounded wait that ran out inside the step
+ * also returns -1; on one GPU the next call starts clean, under tensor
+ * parallelism the model must be closed and reopened on every rank.
  */
 int fwb_forward(fwb_model_t *m, uint32_t token_id, size_t pos, float *logits_host);
 
@@ -275,6 +292,16 @@ int fwb_tp_shard(const char *gguf_path, const char *tensor, int as_head, int ran
 /* Device logits of the last step (n_vocab fp32) and the model's CUDA stream. */
 const float *fwb_logits_dev(fwb_model_t *m);
 void *fwb_stream(fwb_model_t *m);
+
+/*
+ * Page-locked host memory (cudaMallocHost) for logits_host buffers: fwb_forward
+ * then copies the logits straight into it, without the staging copy a pageable
+ * buffer needs.  transformer_b200.c allocates transformer_t.logits this way
+ * (the reference mallocs it, transformer.c:103-115).  NULL on failure;
+ * fwb_host_free accepts NULL.
+ */
+void *fwb_host_alloc(size_t bytes);
+void fwb_host_free(void *p);
 
 #ifdef __cplusplus
 }

@@ -113,8 +113,13 @@ def test_quant_matvec_dev_unaligned_weight_pointer(lib):
     x = gguf_synth.normal_vector(cols, seed=9)
     dx = torch.from_numpy(x).cuda()
     dy = torch.empty(rows, dtype=torch.float32, device="cuda")
+    # the exact row bytes do not reach the 16-byte boundary after the rows: refused
     assert lib.quant_matvec_dev(buf.data_ptr() + 2, w.size, t, dx.data_ptr(), dy.data_ptr(), cols, rows,
+                                None) == -1
+    assert b"16-byte boundary" in lib.fwb_last_error()
+    assert lib.quant_matvec_dev(buf.data_ptr() + 2, w.size + 14, t, dx.data_ptr(), dy.data_ptr(), cols, rows,
                                 None) == 0
+    assert lib.quant_device_status(None) == 0
     torch.cuda.synchronize()
     check_matvec(dy.cpu().numpy(), pyoracle.quant_matvec(w, t, x, rows), _abs_mass(w, t, x, rows))
 
