@@ -19,18 +19,24 @@
 //
 // Arithmetic.  Consumer thread (slot s, unit u) owns columns [64u, 64u+64)
 // of RPT rows per round (independent instruction streams).  Its 64 inputs are
-// held in registers as 16-bit fixed-point integers per 32-block (scale
-// s_b = max|x_b| / 32767), split into two byte planes, so each quant byte
-// feeds dp4a directly:
-//   block dot = d * s_b * (256*A + B - off * sum(xi))
-// with A, B exact integer dot products of the quants with the high (signed)
-// and low byte planes, accumulated by dp4a on top of the bit pattern of
-// 1.5*2^23 so that reading the accumulator as a float and subtracting
-// 1.5*2^23 converts it exactly (|A|, |B| < 2^22) without an int-to-float
-// instruction.  The products and sums are exact; the only rounding is the
-// input's fixed-point representation (at most 1.5e-5 of the block maximum
-// per value; about 3e-6 relative on a block dot of typical inputs) and a few
-// final float operations per block.
+// held in registers as 24-bit fixed-point integers per 32-block
+// (X = rint(x / s_b) rounded once from the exact quotient, scale
+// s_b = max|x_b| / (2^23 - 1)), split into three byte planes
+// (X = 65536*H + 256*M + L; H signed, M and L unsigned), so each quant byte
+// feeds dp4a directly.  Per plane p the block sum
+//   A_p = sum_i (q_i - off) * X_p,i
+// is exact in integers: dp4a adds q_i * X_p,i to an accumulator that starts
+// at the bit pattern of 1.5*2^23 minus off * sum_i X_p,i (a per-block
+// constant of the input), so reading it as a float and subtracting 1.5*2^23
+// converts it exactly (|A_p| < 2^22) without an int-to-float instruction.
+//   block dot = d * s_b * ((256*A_H + A_M)*256 + A_L)
+// where 256*A_H + A_M is exact in fp32 and the outer fma rounds once.  So
+// the only roundings are the input's 24-bit representation (half a unit of
+// 2^-23 of the block maximum per value, the fp32 precision of the block's
+// largest input), one rounding of the block dot, its scale and the sum over
+// blocks -- fewer than the per-element fp32 roundings of the reference's
+// decode-then-dot (quant_matvec.c:243-247); tests/test_gpu_precision.py
+// compares both against an exact product.
 //
 // Reduction.  Rows are processed in batches of 8 per thread; the 8 partial
 // sums are reduced across the unit lanes of a warp with a butterfly
@@ -76,7 +82,9 @@ constexpr uint32_t kHeaderBytes = 1024;  // barriers, stage counters, small scra
 constexpr uint32_t kStageSlack = 128;  // alignment + half-unit over-read room
 constexpr uint32_t kPosUnknown = 0xffffffffu;  // gemv_consume reads the position from step[1]
 constexpr uint32_t kProfSlots = 8;  // GEMV profile values per CTA and phase
-constexpr int kXMax = 32767;        // fixed-point range of the inputs (16 bits per value)
+constexpr int kXMax = 8388607;      // fixed-point range of the inputs (24 bits per value: 2^23 - 1)
+constexpr int kPlanes = 3;          // byte planes of the fixed-point inputs (H, M, L)
+constexpr int kPlaneWords = 8 * kPlanes + 4;  // plane words, 3 accumulator starts and the scale per block
 
 struct GemvArgs {
     uint32_t mode;       // GemvMode (the row loop is shared; only prologue/epilogue differ)
@@ -126,8 +134,8 @@ __device__ __forceinline__ unsigned long long gtime_ns() {
 // input planes
 // ---------------------------------------------------------------------------
 struct XBlock {
-    uint32_t hi[8], lo[8];          // 4 elements per word, element order 4k..4k+3
-    float nx;                       // -OFF * sum(xi)
+    uint32_t hi[8], mid[8], lo[8];  // 4 elements per word, element order 4k..4k+3
+    int ih, im, il;                 // accumulator starts: kMagicBits - OFF * (sum of the plane's digits)
     float s;                        // s_b
 };
 
@@ -137,54 +145,66 @@ constexpr float kMagic = 12582912.0f;
 // ---------------------------------------------------------------------------
 // block dots
 // ---------------------------------------------------------------------------
-// A, B carry the kMagicBits bias (see the header comment)
-__device__ __forceinline__ float finish_block(int A, int B, const XBlock &x, uint32_t dbits) {
-    const float Af = __int_as_float(A) - kMagic, Bf = __int_as_float(B) - kMagic;
-    const float T = fmaf(Af, 256.0f, Bf) + x.nx;
-    return (f16_bits_to_f32(dbits) * x.s) * T;
+// A (high plane), M, B (low plane) carry the kMagicBits bias and already
+// hold the -OFF * sum(X_p) term (see the header comment): the block's integer
+// dot (before the scales) with one rounding.
+__device__ __forceinline__ float finish_block(int A, int M, int B) {
+    const float Af = __int_as_float(A) - kMagic, Mf = __int_as_float(M) - kMagic;
+    const float Bf = __int_as_float(B) - kMagic;
+    return fmaf(fmaf(Af, 256.0f, Mf), 256.0f, Bf);
 }
 
 // Q4_0: 4 quant words (elements 4k..4k+3 in the low nibbles, 16+4k.. in the high)
-__device__ __forceinline__ float dot_q4_0(const uint32_t (&q)[4], uint32_t dbits, const XBlock &x) {
-    int A = kMagicBits, B = kMagicBits;
+__device__ __forceinline__ float dot_q4_0(const uint32_t (&q)[4], const XBlock &x) {
+    int A = x.ih, M = x.im, B = x.il;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         const uint32_t lo = q[k] & 0x0F0F0F0Fu, hi = (q[k] >> 4) & 0x0F0F0F0Fu;
         A = dp4a_us(lo, (int)x.hi[k], A);
         A = dp4a_us(hi, (int)x.hi[k + 4], A);
+        M = dp4a_uu(lo, x.mid[k], M);
+        M = dp4a_uu(hi, x.mid[k + 4], M);
         B = dp4a_uu(lo, x.lo[k], B);
         B = dp4a_uu(hi, x.lo[k + 4], B);
     }
-    return finish_block(A, B, x, dbits);
+    return finish_block(A, M, B);
 }
 
 // spread 4 bits into bit 4 of each byte
 __device__ __forceinline__ uint32_t spread4(uint32_t b) { return ((b & 0xFu) * 0x02040810u) & 0x10101010u; }
 
 // Q5_0: qh = 32-bit high-bit plane (bit j of element j), 4 low-nibble words
-__device__ __forceinline__ float dot_q5_0(uint32_t qh, const uint32_t (&q)[4], uint32_t dbits, const XBlock &x) {
-    int A = kMagicBits, B = kMagicBits;
+__device__ __forceinline__ float dot_q5_0(uint32_t qh, const uint32_t (&q)[4], const XBlock &x) {
+    int A = x.ih, M = x.im, B = x.il;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         const uint32_t lo = (q[k] & 0x0F0F0F0Fu) | spread4(qh >> (4 * k));
         const uint32_t hi = ((q[k] >> 4) & 0x0F0F0F0Fu) | spread4(qh >> (16 + 4 * k));
         A = dp4a_us(lo, (int)x.hi[k], A);
         A = dp4a_us(hi, (int)x.hi[k + 4], A);
+        M = dp4a_uu(lo, x.mid[k], M);
+        M = dp4a_uu(hi, x.mid[k + 4], M);
         B = dp4a_uu(lo, x.lo[k], B);
         B = dp4a_uu(hi, x.lo[k + 4], B);
     }
-    return finish_block(A, B, x, dbits);
+    return finish_block(A, M, B);
 }
 
 // Q8_0: 8 signed quant words
-__device__ __forceinline__ float dot_q8_0(const uint32_t (&q)[8], uint32_t dbits, const XBlock &x) {
-    int A = kMagicBits, B = kMagicBits;
+__device__ __forceinline__ float dot_q8_0(const uint32_t (&q)[8], const XBlock &x) {
+    int A = x.ih, M = x.im, B = x.il;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
         A = dp4a_ss((int)q[k], (int)x.hi[k], A);
+        M = dp4a_su((int)q[k], x.mid[k], M);
         B = dp4a_su((int)q[k], x.lo[k], B);
     }
-    return finish_block(A, B, x, dbits);
+    return finish_block(A, M, B);
+}
+
+// d_b * s_b of a block (fp16 scale bits in the low half of dbits)
+__device__ __forceinline__ float block_scale(uint32_t dbits, const XBlock &x) {
+    return f16_bits_to_f32(dbits) * x.s;
 }
 
 // Words of one unit (two blocks, 2*BB bytes) starting at p (2-byte aligned;
@@ -217,31 +237,31 @@ __device__ __forceinline__ float unit_dot(const uint8_t *p, const XBlock &xa, co
         load_unit_words<9, A4>(p, w);
         uint32_t qa[4] = {__funnelshift_r(w[0], w[1], 16), __funnelshift_r(w[1], w[2], 16),
                           __funnelshift_r(w[2], w[3], 16), __funnelshift_r(w[3], w[4], 16)};
-        const float r = dot_q4_0(qa, w[0], xa);
+        const float r = block_scale(w[0], xa) * dot_q4_0(qa, xa);
         const uint32_t qb[4] = {w[5], w[6], w[7], w[8]};
-        const float r2 = dot_q4_0(qb, w[4] >> 16, xb);
-        return two ? r + r2 : r;
+        const float r2 = fmaf(block_scale(w[4] >> 16, xb), dot_q4_0(qb, xb), r);
+        return two ? r2 : r;
     } else if constexpr (QT == QT_Q5_0) {
         uint32_t w[11];
         load_unit_words<11, A4>(p, w);
         uint32_t qa[4] = {__funnelshift_r(w[1], w[2], 16), __funnelshift_r(w[2], w[3], 16),
                           __funnelshift_r(w[3], w[4], 16), __funnelshift_r(w[4], w[5], 16)};
-        const float r = dot_q5_0(__funnelshift_r(w[0], w[1], 16), qa, w[0], xa);
+        const float r = block_scale(w[0], xa) * dot_q5_0(__funnelshift_r(w[0], w[1], 16), qa, xa);
         const uint32_t qb[4] = {w[7], w[8], w[9], w[10]};
-        const float r2 = dot_q5_0(w[6], qb, w[5] >> 16, xb);
-        return two ? r + r2 : r;
+        const float r2 = fmaf(block_scale(w[5] >> 16, xb), dot_q5_0(w[6], qb, xb), r);
+        return two ? r2 : r;
     } else {
         uint32_t w[17];
         load_unit_words<17, A4>(p, w);
         uint32_t qa[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) qa[k] = __funnelshift_r(w[k], w[k + 1], 16);
-        const float r = dot_q8_0(qa, w[0], xa);
+        const float r = block_scale(w[0], xa) * dot_q8_0(qa, xa);
         uint32_t qb[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) qb[k] = w[9 + k];
-        const float r2 = dot_q8_0(qb, w[8] >> 16, xb);
-        return two ? r + r2 : r;
+        const float r2 = fmaf(block_scale(w[8] >> 16, xb), dot_q8_0(qb, xb), r);
+        return two ? r2 : r;
     }
 }
 
@@ -297,7 +317,8 @@ struct GemvSmem {
     uint32_t *done;   // [kMaxStages] warps finished with the slot, then the refill cursor
     float *misc;      // [64]
     uint32_t *misc_u; // [64]
-    uint32_t *planes; // quantised input: word (p*8+k)*nbp + b (p 0 = high, 1 = low), s at 16*nbp + b, nx at 17*nbp + b
+    uint32_t *planes; // quantised input: word (p*8+k)*nbp + b (p 0 = high, 1 = middle, 2 = low),
+                      // accumulator starts (high, middle, low) at (24+p)*nbp + b, s at 27*nbp + b
     uint32_t nbp;     // blocks of the input, rounded up to even
     float *red;       // partial row sums [local row][warp of the slot]
     uint8_t *ring;
@@ -305,7 +326,7 @@ struct GemvSmem {
 
 // Bytes of the plane area for an input of K values.
 __host__ __device__ constexpr uint32_t plane_bytes(uint32_t K) {
-    return ((18u * (((K / 32) + 1) & ~1u) * 4u) + 127u) & ~127u;
+    return (((uint32_t)kPlaneWords * (((K / 32) + 1) & ~1u) * 4u) + 127u) & ~127u;
 }
 
 // Partial-sum area for n_loc local rows with slots `Upad` threads wide.
@@ -396,23 +417,25 @@ __device__ __forceinline__ void ring_advance(RingState &rs, uint32_t NS) {
 // overlap.  With RMSNorm (rms_norm, norm.c:7-16) the values are multiplied by
 // the norm weight here; the 1/rms factor is a common scale of every block, so
 // it is applied to the block scales afterwards instead of to the values, and
-// x is read once.  Float -> int by adding 1.5*2^23 (exact round-to-nearest
-// for |v| < 2^22).  Ends with a CTA barrier.  Returns the 1/rms factor
+// x is read once.  Float -> int: X = rint(v / s_b) of the exact quotient
+// (up to ties within an ulp), clamped to +-(2^23 - 1).
+// Ends with a CTA barrier.  Returns the 1/rms factor
 // 1/sqrtf(sum(x^2)/K + eps) (IEEE division and square root; every thread
 // sums the warp partials in the same order), or 1 without the norm.
-template <int OFF>
-__device__ float build_planes(const GemvArgs &a, const GemvSmem &sm, uint32_t tid, uint32_t NC, bool prof,
-                              unsigned long long &t_x, unsigned long long &t_b) {
-    constexpr int kPass = 4;
-    const bool norm = a.norm != 0;
+// NP passes of build_planes (below) starting at block b0: every pass's loads
+// are issued before any is used, and the passes have no early exit, so their
+// dependency chains (block maximum, shuffles, rounding) overlap.  Blocks at
+// or beyond nb are predicated off.
+template <int OFF, int NP>
+__device__ __forceinline__ void plane_passes(const GemvArgs &a, const GemvSmem &sm, uint32_t tid, uint32_t b0,
+                                             uint32_t per, bool norm, float &ss, bool prof,
+                                             unsigned long long &t_x) {
     const uint32_t nb = a.K >> 5, nbp = sm.nbp;
-    const uint32_t q = tid & 3, lane = tid & 31, warp = tid >> 5;
-    const uint32_t per = NC >> 2;  // blocks per pass
-    float ss = 0.f;
-    for (uint32_t b0 = 0; b0 < nb; b0 += kPass * per) {
-        float v[kPass][8], wn[kPass][8];
+    const uint32_t q = tid & 3;
+    {
+        float v[NP][8], wn[NP][8];
 #pragma unroll
-        for (int p = 0; p < kPass; ++p) {
+        for (int p = 0; p < NP; ++p) {
             const uint32_t b = b0 + p * per + (tid >> 2);
             const bool on = b < nb;
             const uint32_t c = b * 32 + q * 8;
@@ -428,8 +451,7 @@ __device__ float build_planes(const GemvArgs &a, const GemvSmem &sm, uint32_t ti
             }
         }
 #pragma unroll
-        for (int p = 0; p < kPass; ++p) {
-            if (b0 + p * per >= nb) break;  // uniform over the CTA
+        for (int p = 0; p < NP; ++p) {
             const uint32_t b = b0 + p * per + (tid >> 2);
             const bool on = b < nb;
             if (norm) {
@@ -449,32 +471,81 @@ __device__ float build_planes(const GemvArgs &a, const GemvSmem &sm, uint32_t ti
             m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
             if (prof && b0 == 0 && p == 0) t_x = gtime_ns();  // the first loads have landed
             const bool bad = !isfinite(chk) || !isfinite(m);
-            const float inv = m > 1e-30f && !bad ? (float)kXMax / m : 0.f;
-            int xi[8], sum = 0;
+            const bool zero = !(m > 1e-30f) || bad;
+            // scale slightly above max/kXMax, so |v / sb| <= kXMax
+            const float sb = zero ? 0.f : m * (1.0f / (float)(kXMax - 1));
+            const float inv = zero ? 0.f : __frcp_rn(sb), hsb = 0.5f * sb;
+            int xi[8];
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                xi[j] = __float_as_int(fmaf(v[p][j], inv, kMagic)) - kMagicBits;
-                sum += xi[j];
+                // rint(v / sb) of the exact quotient: a first guess from the
+                // rounded product, then the exact remainder v - X * sb (one
+                // fma) moves it by one where the guess is off
+                int X = __float2int_rn(v[p][j] * inv);
+                const float e = fmaf(-(float)X, sb, v[p][j]);
+                X += (e > hsb) - (e < -hsb);
+                xi[j] = zero ? 0 : min(kXMax, max(-kXMax, X));
             }
-            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+            uint32_t pw[3][2];  // plane words (high, middle, low) of this lane's two groups of 4
+            int sh = 0, sm_ = 0, sl = 0;
+#pragma unroll
+            for (int w = 0; w < 2; ++w) {
+                const int *x4 = xi + 4 * w;
+                // |xi| < 2^23: byte 0 is the low plane, byte 1 the middle, byte 2 the signed high
+                const uint32_t t01 = __byte_perm(x4[0], x4[1], 0x5140), t23 = __byte_perm(x4[2], x4[3], 0x5140);
+                pw[2][w] = __byte_perm(t01, t23, 0x5410);
+                pw[1][w] = __byte_perm(t01, t23, 0x7632);
+                const uint32_t u01 = __byte_perm(x4[0], x4[1], 0x0062), u23 = __byte_perm(x4[2], x4[3], 0x0062);
+                pw[0][w] = __byte_perm(u01, u23, 0x5410);
+                // digit sums of the three planes (dp4a with ones)
+                sh = dp4a_ss((int)pw[0][w], 0x01010101, sh);
+                sm_ = dp4a_uu(pw[1][w], 0x01010101u, sm_);
+                sl = dp4a_uu(pw[2][w], 0x01010101u, sl);
+            }
+#pragma unroll
+            for (int o = 1; o <= 2; o <<= 1) {
+                sh += __shfl_xor_sync(0xffffffffu, sh, o);
+                sm_ += __shfl_xor_sync(0xffffffffu, sm_, o);
+                sl += __shfl_xor_sync(0xffffffffu, sl, o);
+            }
             if (on) {
 #pragma unroll
                 for (int w = 0; w < 2; ++w) {
-                    const int *x4 = xi + 4 * w;
-                    // |xi| <= 32767: byte 0 is the low plane, byte 1 the signed high plane
-                    const uint32_t t01 = __byte_perm(x4[0], x4[1], 0x5140), t23 = __byte_perm(x4[2], x4[3], 0x5140);
-                    const uint32_t lo = __byte_perm(t01, t23, 0x5410), hi = __byte_perm(t01, t23, 0x7632);
                     const uint32_t k = 2 * q + w;
-                    sm.planes[(0 * 8 + k) * nbp + b] = hi;
-                    sm.planes[(1 * 8 + k) * nbp + b] = lo;
+                    sm.planes[(0 * 8 + k) * nbp + b] = pw[0][w];
+                    sm.planes[(1 * 8 + k) * nbp + b] = pw[1][w];
+                    sm.planes[(2 * 8 + k) * nbp + b] = pw[2][w];
                 }
                 if (q == 0) {
-                    sm.planes[16 * nbp + b] = __float_as_uint(bad ? __int_as_float(0x7fc00000)
-                                                                  : (m > 1e-30f ? m * (1.0f / (float)kXMax) : 0.f));
-                    sm.planes[17 * nbp + b] = __float_as_uint((float)(-OFF) * (float)sum);
+                    sm.planes[24 * nbp + b] = (uint32_t)(kMagicBits - OFF * sh);
+                    sm.planes[25 * nbp + b] = (uint32_t)(kMagicBits - OFF * sm_);
+                    sm.planes[26 * nbp + b] = (uint32_t)(kMagicBits - OFF * sl);
+                    sm.planes[27 * nbp + b] = __float_as_uint(bad ? __int_as_float(0x7fc00000) : sb);
                 }
             }
+        }
+        }
+}
+
+template <int OFF>
+__device__ float build_planes(const GemvArgs &a, const GemvSmem &sm, uint32_t tid, uint32_t NC, bool prof,
+                              unsigned long long &t_x, unsigned long long &t_b) {
+    const bool norm = a.norm != 0;
+    const uint32_t nb = a.K >> 5, nbp = sm.nbp;
+    const uint32_t q = tid & 3, lane = tid & 31, warp = tid >> 5;
+    const uint32_t per = NC >> 2;  // blocks per pass
+    float ss = 0.f;
+    for (uint32_t b0 = 0; b0 < nb;) {
+        const uint32_t left = (nb - b0 + per - 1) / per;  // passes still needed
+        if (left >= 3) {
+            plane_passes<OFF, 4>(a, sm, tid, b0, per, norm, ss, prof, t_x);
+            b0 += 4 * per;
+        } else if (left == 2) {
+            plane_passes<OFF, 2>(a, sm, tid, b0, per, norm, ss, prof, t_x);
+            b0 += 2 * per;
+        } else {
+            plane_passes<OFF, 1>(a, sm, tid, b0, per, norm, ss, prof, t_x);
+            b0 += per;
         }
     }
     if (norm) {
@@ -497,15 +568,21 @@ __device__ __forceinline__ void load_planes(const GemvSmem &sm, uint32_t unit, f
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
         const uint2 h = *reinterpret_cast<const uint2 *>(sm.planes + (0 * 8 + k) * nbp + b);
-        const uint2 l = *reinterpret_cast<const uint2 *>(sm.planes + (1 * 8 + k) * nbp + b);
+        const uint2 md = *reinterpret_cast<const uint2 *>(sm.planes + (1 * 8 + k) * nbp + b);
+        const uint2 l = *reinterpret_cast<const uint2 *>(sm.planes + (2 * 8 + k) * nbp + b);
         xa.hi[k] = h.x; xb.hi[k] = h.y;
+        xa.mid[k] = md.x; xb.mid[k] = md.y;
         xa.lo[k] = l.x; xb.lo[k] = l.y;
     }
-    const uint2 sv = *reinterpret_cast<const uint2 *>(sm.planes + 16 * nbp + b);
-    const uint2 nv = *reinterpret_cast<const uint2 *>(sm.planes + 17 * nbp + b);
+    const uint2 ih = *reinterpret_cast<const uint2 *>(sm.planes + 24 * nbp + b);
+    const uint2 im = *reinterpret_cast<const uint2 *>(sm.planes + 25 * nbp + b);
+    const uint2 il = *reinterpret_cast<const uint2 *>(sm.planes + 26 * nbp + b);
+    const uint2 sv = *reinterpret_cast<const uint2 *>(sm.planes + 27 * nbp + b);
+    xa.ih = (int)ih.x; xb.ih = (int)ih.y;
+    xa.im = (int)im.x; xb.im = (int)im.y;
+    xa.il = (int)il.x; xb.il = (int)il.y;
     xa.s = __fmul_rn(__uint_as_float(sv.x), scale);
     xb.s = __fmul_rn(__uint_as_float(sv.y), scale);
-    xa.nx = __uint_as_float(nv.x); xb.nx = __uint_as_float(nv.y);
 }
 
 // RoPE of one adjacent pair (rope.c:37-43).

@@ -11,6 +11,18 @@ quant_gguf_py.npz
     reference has no Q4_0 decoder) and the Q5_0 / Q8_0 decoders against an
     independent implementation of the GGML formats.
 
+ref_full_<model>.npz   (python tests/golden/make_golden.py full <model>)
+    The compiled reference at the benchmark configurations, full depth: the
+    Llama-3-8B-shaped Q4_0 model (the bench's model: same seed), the 8B mixed
+    Q8_0/Q5_0 model after an 8000-position K/V pre-fill (fp16-rounded N(0,1),
+    prefill_kv), and the first 8 layers of the Llama-70B-shaped Q4_0 model
+    with its full 128256-entry vocabulary.  An 8-token seeded prompt goes
+    through transformer_forward one token at a time, then 64 greedy steps.
+    Stored: the model's sha256, the prompt, the 64 greedy tokens, per step
+    the 32 largest logits (index and value) and the logits' L2 norm, and the
+    full logits row at steps 0, 31 and 63.  Each model takes minutes to
+    hours of single-threaded reference time.
+
 ref_decode_<model>.npz
     The compiled reference's own transformer_forward (oracle/_ref) on seeded
     synthetic GGUFs: the sha256 of the model bytes, the greedy token stream
@@ -109,8 +121,70 @@ def make_decode(tmp: str):
                                 tokens=np.array(toks, np.uint32), logits=np.stack(logits))
 
 
+# full-depth models of the benchmark configurations: (shape, seed, K/V
+# pre-fill positions, kv_ctx)
+FULL_MODELS = {
+    "llama8b_q4_0": (configs.LLAMA8B_Q4_0, 1, 0, 128),
+    "llama8b_mixed": (configs.LLAMA8B_MIXED, 1, 8000, 8192),
+    "llama70b_q4_0_8layer": (configs.with_layers(configs.LLAMA70B_Q4_0, 8), 1, 0, 128),
+}
+FULL_PROMPT = 8
+FULL_STEPS = 64
+FULL_TOPK = 32
+FULL_ROWS = (0, 31, 63)  # steps whose whole logits row is stored
+
+
+def full_prompt(cfg, seed: int) -> np.ndarray:
+    return np.random.default_rng(seed + 77).integers(0, cfg.n_vocab, FULL_PROMPT).astype(np.uint32)
+
+
+def topk(lg: np.ndarray, k: int = FULL_TOPK) -> tuple[np.ndarray, np.ndarray]:
+    """Indices (value descending, index ascending on ties) and values."""
+    idx = np.lexsort((np.arange(lg.size), -lg.astype(np.float64)))[:k]
+    return idx.astype(np.uint32), lg[idx]
+
+
+def make_full(tag: str, directory: str) -> str:
+    """Golden of one full-depth model (see the module docstring)."""
+    import pyoracle
+    cfg, seed, n_pre, kv_ctx = FULL_MODELS[tag]
+    path = gguf_synth.cached_model(cfg, seed=seed, directory=directory)
+    ref = pyoracle.RefModel(path, kv_ctx)
+    for layer in range(cfg.n_layer if n_pre else 0):
+        k, v = prefill_kv(cfg, layer, n_pre, seed)
+        ref.kv_load(layer, 0, k, v)
+    prompt = full_prompt(cfg, seed)
+    pos = n_pre
+    for t in prompt[:-1]:
+        ref.forward(int(t), pos)
+        pos += 1
+    tok = int(prompt[-1])
+    toks, tidx, tval, norms, rows = [], [], [], [], []
+    for i in range(FULL_STEPS):
+        lg = ref.forward(tok, pos + i)
+        a, b = topk(lg)
+        tidx.append(a)
+        tval.append(b)
+        norms.append(np.linalg.norm(lg.astype(np.float64)))
+        if i in FULL_ROWS:
+            rows.append(lg.copy())
+        tok = int(np.argmax(lg))
+        toks.append(tok)
+        print(f"{tag}: step {i} token {tok}", flush=True)
+    ref.close()
+    out = os.path.join(HERE, f"ref_full_{tag}.npz")
+    np.savez_compressed(out, sha256=np.array(sha256(path)), seed=np.array(seed), n_prefill=np.array(n_pre),
+                        kv_ctx=np.array(kv_ctx), prompt=prompt, pos_first=np.array(pos),
+                        tokens=np.array(toks, np.uint32), top_idx=np.stack(tidx), top_val=np.stack(tval),
+                        norm=np.array(norms), row_steps=np.array(FULL_ROWS), rows=np.stack(rows))
+    return out
+
+
 if __name__ == "__main__":
     import tempfile
+    if len(sys.argv) > 2 and sys.argv[1] == "full":
+        print("written", make_full(sys.argv[2], sys.argv[3] if len(sys.argv) > 3 else "/tmp/fwb_models"))
+        sys.exit(0)
     make_quant()
     with tempfile.TemporaryDirectory() as tmp:
         make_decode(tmp)
