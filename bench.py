@@ -70,40 +70,65 @@ class Workload:
     N > 1: configuration 5 -- the Llama-70B shape, every linear weight Q4_0,
     256-token prompt, greedy decode tensor-parallel over the N GPUs (one
     decode stream for the whole box: strong scaling).
+    --workload long-context (N = 1): configuration 4 -- the 8B shape with
+    Q8_0 attention / down / head and Q5_0 gate / up, context 8192 with the
+    K/V cache pre-filled at positions [0, 8000) with fp16-rounded N(0, 1)
+    values, then greedy decode from position 8000.
     """
 
-    def __init__(self, world: int, layers: int = 0):
+    def __init__(self, world: int, layers: int = 0, kind: str = "default"):
         self.tp = world > 1
-        self.base = configs.LLAMA70B_Q4_0 if self.tp else configs.LLAMA8B_Q4_0
+        self.long = kind == "long-context"
+        if self.long and self.tp:
+            raise SystemExit("--workload long-context runs on one GPU")
+        self.base = (configs.LLAMA8B_MIXED if self.long else
+                     configs.LLAMA70B_Q4_0 if self.tp else configs.LLAMA8B_Q4_0)
         self.cfg = configs.with_layers(self.base, layers) if layers else self.base
-        self.prompt = 256 if self.tp else 512
-        shape = "Llama-70B" if self.tp else "Llama-3-8B"
-        feed = "one decode step per token" if self.tp else "fwb_prefill"
+        self.prompt = 8000 if self.long else 256 if self.tp else 512
+        if self.long:
+            shape = "Llama-3-8B-shaped decoder, Q8_0 attention/down/head and Q5_0 gate/up"
+            feed = "K/V cache pre-filled at 8000 positions with fp16-rounded N(0,1) values (fwb_kv_load)"
+        else:
+            shape = ("Llama-70B" if self.tp else "Llama-3-8B") + "-shaped decoder, all linear weights Q4_0"
+            feed = f"{self.prompt}-token random prompt (" + ("one decode step per token" if self.tp
+                                                            else "fwb_prefill") + ")"
         if layers:
             shape += f" (first {layers} layers only: a profiler case, not a bench value)"
-        self.text = (f"{shape}-shaped decoder, all linear weights Q4_0, fp32 embedding/norms, "
-                     f"random-init N(0,0.02); {self.prompt}-token random prompt ({feed}), then "
+        self.text = (f"{shape}, fp32 embedding/norms, random-init N(0,0.02); {feed}, then "
                      f"greedy decode at batch 1" + (f", tensor parallel over {world} GPUs" if self.tp else ""))
 
     def prompt_ids(self) -> np.ndarray:
+        if self.long:  # no prompt tokens: the first decode step is fed this token
+            return np.array([1], dtype=np.uint32)
         return np.random.default_rng(PROMPT_SEED).integers(0, self.cfg.n_vocab, self.prompt).astype(np.uint32)
+
+    def kv_prefill(self, load) -> None:
+        """load(layer, pos0, k, v) for the long-context pre-fill (no-op otherwise)."""
+        if not self.long:
+            return
+        for layer in range(self.cfg.n_layer):
+            k, v = gguf_synth.kv_prefill_values(self.cfg, layer, self.prompt, MODEL_SEED)
+            load(layer, 0, k, v)
 
     def kv_bytes_per_position(self, world: int = 1) -> int:
         c = self.cfg
         return 2 * c.n_layer * (c.n_head_kv // world) * c.head_dim * 4
 
     def config(self, world: int, k_steps: int, w_steps: int, kv_ctx: int) -> dict:
-        return {
+        cfg = {
             "workload": self.text,
             "model": self.cfg.name,
             "global_batch": 1,
-            "prompt_tokens": self.prompt,
+            "prompt_tokens": 0 if self.long else self.prompt,
             "decode_positions": [self.prompt + w_steps, self.prompt + w_steps + k_steps],
             "kv_ctx": kv_ctx,
             "parallelism": f"tensor parallel x{world}" if world > 1 else "single GPU",
             "l2": "inputs larger than L2: every step streams the model's quantised weights "
                   f"({self.cfg.weight_bytes_per_token() / 1e9:.1f} GB per token)",
         }
+        if self.long:
+            cfg["kv_prefill_positions"] = self.prompt
+        return cfg
 
 
 def _args():
@@ -121,6 +146,8 @@ def _args():
     p.add_argument("--model-dir", default=None, help="where the synthetic GGUF is cached")
     p.add_argument("--layers", type=int, default=0,
                    help="profiler case: the same model with only its first N layers (not a bench value)")
+    p.add_argument("--workload", choices=("default", "long-context"), default="default",
+                   help="long-context: benchmark configuration 4 (8B mixed quants, 8000 pre-filled positions)")
     return p.parse_args()
 
 
@@ -146,9 +173,12 @@ def _model_path(args, wl: Workload) -> str:
 
 
 def _kv_ctx(wl: Workload, k_steps: int, w_steps: int) -> int:
-    """KV length both arms allocate: the prompt, the warm-up and the timed
-    decode steps of the b200 arm (which decodes twice: device-timed, then e2e)."""
-    need = wl.prompt + 2 * (w_steps + k_steps) + 1
+    """KV length both arms allocate: the prompt (or pre-filled positions),
+    the warm-up and the timed decode steps (the b200 arm's e2e pass decodes
+    the timed positions again)."""
+    if wl.long:
+        return 8192
+    need = wl.prompt + w_steps + k_steps + 1
     return max(1024, 1 << (need - 1).bit_length())
 
 
@@ -233,11 +263,14 @@ def _time_reference(path: str, wl: Workload, kv_ctx: int, warm: int, n_max: int,
     Returns (tokens/s, steps timed, kind, seconds, first timed position)."""
     c, P = wl.cfg, wl.prompt
     ref, kind = _reference_model(path, kv_ctx)
-    rng = np.random.default_rng(7)
-    for layer in range(c.n_layer):
-        k = rng.standard_normal((P, c.n_head_kv, c.head_dim), dtype=np.float32)
-        v = rng.standard_normal((P, c.n_head_kv, c.head_dim), dtype=np.float32)
-        ref.kv_load(layer, 0, k, v)
+    if wl.long:
+        wl.kv_prefill(ref.kv_load)
+    else:
+        rng = np.random.default_rng(7)
+        for layer in range(c.n_layer):
+            k = rng.standard_normal((P, c.n_head_kv, c.head_dim), dtype=np.float32)
+            v = rng.standard_normal((P, c.n_head_kv, c.head_dim), dtype=np.float32)
+            ref.kv_load(layer, 0, k, v)
     tok, pos = int(wl.prompt_ids()[-1]), P
     for _ in range(warm):
         tok = int(np.argmax(ref.forward(tok, pos)))
@@ -260,7 +293,7 @@ def run_reference(args) -> None:
     rank, world, _ = _dist()
     if rank != 0:
         return
-    wl = Workload(args.gpus, args.layers)
+    wl = Workload(args.gpus, args.layers, args.workload)
     path = _model_path(args, wl)
     K, W = args.steps, args.warmup
     kv_ctx = _kv_ctx(wl, K, W)
@@ -295,7 +328,7 @@ def run_b200(args) -> None:
     rank, world, local = _dist()
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
-    wl = Workload(world, args.layers)
+    wl = Workload(world, args.layers, args.workload)
     torch.cuda.set_device(local)
     if world > 1:
         # host coordination only (IPC handles, barriers, the max over ranks):
@@ -336,7 +369,10 @@ def run_b200(args) -> None:
     # main loop.
     prefill = None
     prompt = wl.prompt_ids()
-    if world == 1:
+    if wl.long:
+        wl.kv_prefill(m.kv_load)
+        tok = int(prompt[0])
+    elif world == 1:
         m.prefill(prompt, 0)
         torch.cuda.synchronize()
         t0 = time.perf_counter()
@@ -383,9 +419,12 @@ def run_b200(args) -> None:
     tok, pos = int(toks[-1]), pos + K
 
     # ---- end to end through fwb_forward with host buffers (every rank gets
-    # ---- the full logits and picks the same token)
+    # ---- the full logits and picks the same token), over the same positions
+    # ---- as the device-timed pass (a few warm-up positions before them)
     logits = torch.empty(m.n_vocab, dtype=torch.float32, pin_memory=True).numpy()
-    for _ in range(min(W, 3)):  # first use of the pinned logits path
+    w2 = min(W, 3)
+    pos = pos_timed - w2
+    for _ in range(w2):  # first use of the pinned logits path
         m.forward(tok, pos, out=logits)
         tok, pos = int(np.argmax(logits)), pos + 1
     barrier()

@@ -181,6 +181,17 @@ def random_matrix(t: int, rows: int, cols: int, seed: int, mode: int = 1,
     return buf
 
 
+def kv_prefill_values(cfg: ModelShape, layer: int, n: int, seed: int) -> tuple[np.ndarray, np.ndarray]:
+    """K and V rows [n][n_head_kv][head_dim] of one layer for a K/V cache
+    pre-fill: N(0, 1) rounded to fp16 (benchmark configuration 4), seeded
+    per (seed, layer)."""
+    rng = np.random.default_rng(seed * 1000 + layer)
+    shape = (n, cfg.n_head_kv, cfg.head_dim)
+    k = rng.standard_normal(shape).astype(np.float16).astype(np.float32)
+    v = rng.standard_normal(shape).astype(np.float16).astype(np.float32)
+    return k, v
+
+
 def normal_vector(n: int, seed: int, mean: float = 0.0, sd: float = 1.0) -> np.ndarray:
     lib = native.synth_lib()
     out = np.empty(n, dtype=np.float32)

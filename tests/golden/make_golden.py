@@ -65,11 +65,7 @@ def sha256(path: str) -> str:
 
 
 def prefill_kv(cfg, layer: int, n: int, seed: int):
-    rng = np.random.default_rng(seed * 1000 + layer)
-    shape = (n, cfg.n_head_kv, cfg.head_dim)
-    k = rng.standard_normal(shape).astype(np.float16).astype(np.float32)
-    v = rng.standard_normal(shape).astype(np.float16).astype(np.float32)
-    return k, v
+    return gguf_synth.kv_prefill_values(cfg, layer, n, seed)
 
 
 def make_quant():
