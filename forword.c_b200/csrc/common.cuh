@@ -22,7 +22,25 @@ enum : uint32_t {
     ERR_BAD_TOKEN = 1u << 4,    // token id outside the vocabulary
     ERR_ATTN_TIMEOUT = 1u << 5,
     ERR_GRID_SYNC = 1u << 6,     // a grid barrier of the persistent kernel timed out
+    ERR_EXCHANGE = 1u << 7,      // a rank's tagged partial sums did not arrive (tensor parallelism)
 };
+
+// Tensor parallelism: ranks of one box.
+constexpr uint32_t kMaxRanks = 8;
+
+// Tagged 8-byte words of the cross-rank exchange: value bits in the low
+// half, the exchange's tag in the high half, written and read as one
+// single-copy-atomic 8-byte access, so a reader that sees the tag sees the
+// value with it and no fence is needed between them.
+__device__ __forceinline__ void st_tagged(unsigned long long *p, float v, uint32_t tag) {
+    const unsigned long long w = ((unsigned long long)tag << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_tagged(const unsigned long long *p) {
+    unsigned long long w;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
 
 // Upper bound on polls of one barrier phase.  With the back-off below this is
 // several seconds, far beyond any legitimate wait inside one decode step.

@@ -32,11 +32,13 @@ struct EmbedArgs {
 // straight from every rank's exchange buffer over NVLink (peer pointers; no
 // multicast), added to the residual x.  Every rank sums in rank order, so all
 // ranks hold bit-identical x afterwards.
-constexpr uint32_t kMaxRanks = 8;
 struct ArArgs {
     float *x;                      // [n] residual stream of this rank (x += sum of parts)
-    const float *part[kMaxRanks];  // every rank's partial output of this phase
+    const unsigned long long *in;  // this rank's receive slot: [rank q][n] tagged partials
+    const uint32_t *epoch;         // exchange epoch of the step (tags are epoch + k + 1)
+    uint32_t k;                    // index of this exchange within the step
     uint32_t n, world;
+    uint32_t *err, *abort;
 };
 // Tensor parallelism: the greedy token from the ranks' (value, index)
 // candidates (lowest index among equal maxima, as sampler_argmax).
@@ -52,6 +54,7 @@ struct __align__(16) Phase {
     uint32_t kind, qt, mode, a4;  // PH_GEMV: quant type, mode, 4-byte-aligned units
     uint32_t hd, gq;              // PH_ATTN: head_dim, GQA group
     uint32_t gsync;               // the barrier before this phase spans every rank
+    uint32_t nobar;               // no grid barrier before this phase (it waits on tagged data)
     GemvArgs g;
     AttnArgs at;
     EmbedArgs e;
@@ -88,7 +91,8 @@ struct DecodeArgs {
     // n_gsync at the end of the step by CTA 0)
     unsigned long long *gcount[kMaxRanks];
     unsigned long long *gbase;
-    uint32_t world, n_gsync;
+    uint32_t *xepoch;      // exchange epoch: advanced by n_exchange at the end of the step by CTA 0
+    uint32_t world, n_gsync, n_exchange;
     unsigned long long *trace;  // optional: CTA 0's globaltimer at phase start [2p] and barrier arrival [2p+1]
     unsigned long long *trace_cta;  // optional: every CTA's barrier arrival [p * gridDim.x + cta]
 };
@@ -259,20 +263,40 @@ __device__ bool global_sync(const DecodeArgs &d, unsigned long long nb, uint32_t
     return ok_flag != 0;
 }
 
-// x[i] += sum over ranks of part_q[i] for this CTA's rows (peer loads bypass L1).
-__device__ void allreduce_phase(const ArArgs &a) {
+// x[i] += sum over ranks of part_q[i] for this CTA's rows.  Every rank's
+// GEMV epilogue pushed its partial rows into this rank's receive slot as
+// tagged words (GM_PUSH); here each row waits for the W tags of this
+// exchange (bounded polling of local memory: no barrier and no fence), then
+// the partials are added in rank order, so every rank computes bit-identical
+// x.  Returns false if a tag did not arrive (error word and abort flag set).
+__device__ bool allreduce_phase(const ArArgs &a) {
     const uint32_t b = (uint32_t)((uint64_t)blockIdx.x * a.n / gridDim.x);
     const uint32_t e = (uint32_t)((uint64_t)(blockIdx.x + 1) * a.n / gridDim.x);
+    const uint32_t tag = __ldcg(a.epoch) + a.k + 1;
+    bool ok = true;
     for (uint32_t i = b + threadIdx.x; i < e; i += blockDim.x) {
-        float v[kMaxRanks];
-#pragma unroll
-        for (uint32_t q = 0; q < kMaxRanks; ++q) v[q] = q < a.world ? __ldcg(a.part[q] + i) : 0.f;
-        float t = v[0];
-#pragma unroll
-        for (uint32_t q = 1; q < kMaxRanks; ++q)
-            if (q < a.world) t = __fadd_rn(t, v[q]);
+        float t = 0.f;
+        for (uint32_t q = 0; q < a.world; ++q) {
+            const unsigned long long *p = a.in + (size_t)q * a.n + i;
+            unsigned long long w = ld_tagged(p);
+            for (uint32_t it = 0; (uint32_t)(w >> 32) != tag; ++it) {
+                if (it >= kMaxPolls || (it % 1024 == 1023 && *(volatile uint32_t *)a.abort)) {
+                    atomicOr(a.err, ERR_EXCHANGE);
+                    atomicExch(a.abort, 1u);
+                    ok = false;
+                    break;
+                }
+                if (it > 64) __nanosleep(64);
+                w = ld_tagged(p);
+            }
+            if (!ok) break;
+            const float v = __uint_as_float((uint32_t)w);
+            t = q == 0 ? v : __fadd_rn(t, v);
+        }
+        if (!ok) break;
         a.x[i] = __fadd_rn(__ldcg(&a.x[i]), t);
     }
+    return __syncthreads_and(ok) != 0;
 }
 
 __device__ void tp_argmax_phase(const TpArgmaxArgs &a) {
@@ -388,7 +412,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel_t(const __gri
     const uint32_t pos = __ldcg(&d.step[1]);
     // cross-rank barriers completed before this step, and during it
     const unsigned long long gbase = d.world > 1 ? __ldcg(d.gbase) : 0ull;
-    uint32_t gk = 0;
+    uint32_t gk = 0, nbar = 0;
     bool ok = true;
     // phase descriptors are staged in shared memory one phase ahead
     __shared__ __align__(16) Phase ph_buf[2];
@@ -430,7 +454,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel_t(const __gri
                 if constexpr (AHD != 0) attn_phase_t<AHD, AGQ>(P.at, smem + kHeaderBytes, pos);
                 else attn_phase(P, smem + kHeaderBytes, pos);
             } else if (P.kind == PH_ALLREDUCE) {
-                allreduce_phase(P.ar);
+                if (!allreduce_phase(P.ar)) ok = false;
             } else if (P.kind == PH_TPARGMAX) {
                 tp_argmax_phase(P.am);
             } else {  // PH_EMBED: x = row step[0] of the table (linear_get_row, linear.c:60-151)
@@ -463,7 +487,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel_t(const __gri
             // barrier and then the cross-rank one (grid_sync counts epochs by
             // phase index)
             __syncthreads();
-            if (!grid_sync(d.sync, p + 1, d.err, &N, pos)) ok = false;
+            if (!N.nobar && !grid_sync(d.sync, ++nbar, d.err, &N, pos)) ok = false;
             if (N.gsync) {
                 ++gk;
                 if (!global_sync(d, gbase + gk, gk)) ok = false;
@@ -471,8 +495,11 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel_t(const __gri
         }
     }
     if (d.trace && blockIdx.x == 0 && tid == 0) d.trace[2 * d.n_ph] = global_ns();
-    // every CTA read gbase before the first barrier of the step
-    if (d.world > 1 && blockIdx.x == 0 && tid == 0) *d.gbase = gbase + d.n_gsync;
+    // every CTA read gbase and the exchange epoch before the step's last barrier
+    if (d.world > 1 && blockIdx.x == 0 && tid == 0) {
+        *d.gbase = gbase + d.n_gsync;
+        *d.xepoch = __ldcg(d.xepoch) + d.n_exchange;
+    }
     if (!ok && tid == 0) ring_drain(sm, min(total, rs.j + d.NS), d.NS, d.err);
 }
 

@@ -72,6 +72,7 @@ enum GemvMode : int {
     GM_QKV = 2,     // rows [q | k | v]: RoPE on q, k; k, v appended to the KV cache
     GM_SWIGLU = 3,  // y[i]  = silu((Wg x)[i]) * (Wu x)[i]
     GM_LOGITS = 4,  // y[r]  = (W x)[r], plus the grid-wide greedy argmax
+    GM_PUSH = 5,    // (W x)[r] sent to every rank as a tagged word (tensor-parallel partial sums)
 };
 enum InMode : int { IN_PLAIN = 0, IN_RMSNORM = 1 };
 
@@ -116,6 +117,10 @@ struct GemvArgs {
     uint32_t idx_base;     // GM_LOGITS: vocabulary index of row 0 (a tensor-parallel rank's slice)
     float *tp_cand;        // GM_LOGITS under tensor parallelism: (value, index) of this rank's
                            // maximum goes here instead of advancing the step
+    // GM_PUSH: row r goes to ll_out[q][r] of every rank q (tag: *ll_epoch + ll_k + 1)
+    unsigned long long *ll_out[kMaxRanks];
+    const uint32_t *ll_epoch;
+    uint32_t ll_k, world;
     uint32_t *err;
     // optional profile: thread 0 of each CTA adds ns spent in
     // [0] prologue (norm + planes), [1] waiting for stages, [2] the row loop, [3] tail,
@@ -632,6 +637,8 @@ __device__ bool gemv_consume(const GemvArgs &a, const GemvSmem &sm, uint32_t tid
     uint32_t pos = 0;
     if (MODE == GM_RESID && tid < n_loc) pre_y = __ldcg(&a.y[rb + tid]);
     if (MODE == GM_QKV) pos = pos_known != kPosUnknown ? pos_known : __ldcg(&a.step[1]);
+    uint32_t ll_tag = 0;
+    if (MODE == GM_PUSH) ll_tag = __ldcg(a.ll_epoch) + a.ll_k + 1;
 
     unsigned long long t_x = 0ull, t_b = 0ull;
     const float rscale = build_planes<OFF>(a, sm, tid, NC, prof, t_x, t_b);
@@ -752,6 +759,11 @@ __device__ bool gemv_consume(const GemvArgs &a, const GemvSmem &sm, uint32_t tid
                     const uint32_t gi = a.idx_base + g;
                     if (t > best_v || (t == best_v && gi < best_i)) { best_v = t; best_i = gi; }
                 }
+            }
+        } else if (MODE == GM_PUSH) {
+            for (uint32_t i = tid; i < n_loc; i += NC) {
+                const float t = row_sum(i);
+                for (uint32_t q = 0; q < a.world; ++q) st_tagged(a.ll_out[q] + rb + i, t, ll_tag);
             }
         } else if (MODE == GM_SWIGLU) {
             for (uint32_t i = tid; 2 * i < n_loc; i += NC)

@@ -688,9 +688,10 @@ static bool load_model(fwb_model *m, const char *path, size_t max_ctx) {
     if (W > 1) {
         // exchange buffer, mapped by every other rank: [0] cross-rank barrier
         // counter (u64), [256] (value, index) argmax candidate, [512] two
-        // partial-output slots of n_embd floats, then this rank's logits
+        // receive slots of world x n_embd tagged partial sums (8 bytes each;
+        // exchanges alternate between the slots), then this rank's logits
         m->x_part = 512;
-        m->x_logits = (512 + 2ull * E * 4 + 255) / 256 * 256;
+        m->x_logits = (512 + 2ull * W * E * 8 + 255) / 256 * 256;
         m->xbytes = m->x_logits + (uint64_t)Vr * 4 + 256;
         if (!dalloc(m, (void **)&m->xbuf, m->xbytes) || !dalloc(m, (void **)&m->gbase, 64)) return false;
         m->logits = reinterpret_cast<float *>(m->xbuf + m->x_logits);
@@ -703,7 +704,7 @@ static bool load_model(fwb_model *m, const char *path, size_t max_ctx) {
         !dalloc(m, (void **)&m->vc, kvn * 4) ||
         !dalloc(m, (void **)&m->rope_cos, (size_t)m->kv_ctx * (hd / 2) * 4 + 4) ||
         !dalloc(m, (void **)&m->rope_sin, (size_t)m->kv_ctx * (hd / 2) * 4 + 4) ||
-        !dalloc(m, (void **)&m->step, 64) ||
+        !dalloc(m, (void **)&m->step, 64) || !dalloc(m, (void **)&m->sync, 64) ||
         !dalloc(m, (void **)&m->hist, (size_t)m->kv_ctx * 4 + 4) ||
         !dalloc(m, (void **)&m->am_val, 4096 * 4) || !dalloc(m, (void **)&m->am_idx, 4096 * 4) ||
         !dalloc(m, (void **)&m->am_ticket, 64) || !dalloc(m, (void **)&m->attn_ticket, 4 * KVr + 64))
@@ -746,23 +747,39 @@ static bool build_steps(fwb_model *m) {
     // per rank under tensor parallelism (world 1: the whole model)
     const uint32_t W = m->world, Hr = H / W, KVr = KV / W, Fr = F / W, Vr = c.n_vocab / W;
     const size_t layer_kv = (size_t)KVr * m->kv_ctx * hd;
-    uint32_t n_ar = 0;  // all-reduces so far (their partial slots alternate)
-    // sum of every rank's partial output into x, after a cross-rank barrier
+    uint32_t n_ar = 0;  // exchanges so far this step (their receive slots alternate)
+    const uint64_t slot_bytes = (uint64_t)W * E * 8;
+    // the sum of every rank's partial output into x: each row waits for the
+    // ranks' tagged partials in this rank's receive slot (no barrier before it)
     auto allreduce_step = [&](const std::string &name) {
         Step s;
         s.name = name;
         s.phase.kind = PH_ALLREDUCE;
-        s.phase.gsync = 1;
+        s.phase.nobar = 1;
         s.phase.ar.x = m->x;
         s.phase.ar.n = E;
         s.phase.ar.world = W;
-        for (uint32_t q = 0; q < W; ++q)
-            s.phase.ar.part[q] = reinterpret_cast<const float *>(m->peer[q] + m->x_part + (uint64_t)(n_ar & 1) * E * 4);
+        s.phase.ar.in = reinterpret_cast<const unsigned long long *>(m->xbuf + m->x_part + (n_ar & 1) * slot_bytes);
+        s.phase.ar.epoch = reinterpret_cast<const uint32_t *>(m->gbase + 1);
+        s.phase.ar.k = n_ar;
+        s.phase.ar.err = m->err;
+        s.phase.ar.abort = m->sync + 1;
         s.run = [](cudaStream_t, bool) { return cudaErrorNotSupported; };
         m->steps.push_back(std::move(s));
         ++n_ar;
     };
-    auto part_out = [&]() { return reinterpret_cast<float *>(m->xbuf + m->x_part + (uint64_t)(n_ar & 1) * E * 4); };
+    // GEMV arguments of a partial-output phase: rows pushed to every rank's
+    // receive slot (this rank's block of it)
+    auto push_args = [&]() {
+        GemvArgs ex{};
+        for (uint32_t q = 0; q < W; ++q)
+            ex.ll_out[q] = reinterpret_cast<unsigned long long *>(m->peer[q] + m->x_part + (n_ar & 1) * slot_bytes +
+                                                                  (uint64_t)m->rank * E * 8);
+        ex.ll_epoch = reinterpret_cast<const uint32_t *>(m->gbase + 1);
+        ex.ll_k = n_ar;
+        ex.world = W;
+        return ex;
+    };
     m->steps.clear();
     if (const char *hr = getenv("FWB_HALF_ROWS"))  // (testing: the two-row stages on any model)
         if (*hr == '1' && m->persistent) m->half_rows = true;
@@ -882,7 +899,7 @@ static bool build_steps(fwb_model *m) {
             if (!gemv_step(p + "o_proj_resid", GM_RESID, w.o, nullptr, E, m->att, nullptr, m->x, GemvArgs{}))
                 return false;
         } else {  // this rank's heads' share of o-proj, then the all-reduce into x
-            if (!gemv_step(p + "o_proj_part", GM_STORE, w.o, nullptr, E, m->att, nullptr, part_out(), GemvArgs{}))
+            if (!gemv_step(p + "o_proj_part", GM_PUSH, w.o, nullptr, E, m->att, nullptr, nullptr, push_args()))
                 return false;
             allreduce_step(p + "o_proj_allreduce");
         }
@@ -892,7 +909,7 @@ static bool build_steps(fwb_model *m) {
             if (!gemv_step(p + "down_resid", GM_RESID, w.down, nullptr, E, m->h, nullptr, m->x, GemvArgs{}))
                 return false;
         } else {
-            if (!gemv_step(p + "down_part", GM_STORE, w.down, nullptr, E, m->h, nullptr, part_out(), GemvArgs{}))
+            if (!gemv_step(p + "down_part", GM_PUSH, w.down, nullptr, E, m->h, nullptr, nullptr, push_args()))
                 return false;
             allreduce_step(p + "down_allreduce");
         }
@@ -1044,7 +1061,7 @@ static bool build_decode(fwb_model *m) {
     StageSrc *d_tab;
     uint32_t *d_nst;
     if (!dalloc(m, (void **)&d_ph, ph.size() * sizeof(Phase)) || !dalloc(m, (void **)&d_tab, tab.size() * sizeof(StageSrc)) ||
-        !dalloc(m, (void **)&d_nst, G * 4) || !dalloc(m, (void **)&m->sync, 64))
+        !dalloc(m, (void **)&d_nst, G * 4))
         return false;
     CK(cudaMemcpy(d_ph, ph.data(), ph.size() * sizeof(Phase), cudaMemcpyHostToDevice));
     CK(cudaMemcpy(d_tab, tab.data(), tab.size() * sizeof(StageSrc), cudaMemcpyHostToDevice));
@@ -1063,8 +1080,13 @@ static bool build_decode(fwb_model *m) {
     d.n_st_cta = d_nst;
     d.world = m->world;
     d.gbase = m->gbase;
+    d.xepoch = m->gbase ? reinterpret_cast<uint32_t *>(m->gbase + 1) : nullptr;
     d.n_gsync = 0;
-    for (const Phase &p : ph) d.n_gsync += p.gsync;
+    d.n_exchange = 0;
+    for (const Phase &p : ph) {
+        d.n_gsync += p.gsync;
+        d.n_exchange += p.kind == PH_ALLREDUCE ? 1u : 0u;
+    }
     if (m->world > 1) {  // [0] is this rank's own counter
         d.gcount[0] = reinterpret_cast<unsigned long long *>(m->xbuf);
         for (uint32_t q = 0, k = 1; q < m->world; ++q)
