@@ -360,7 +360,10 @@ def run_b200(args) -> None:
     if kv_ctx > wl.cfg.n_ctx:
         raise SystemExit(f"--steps/--warmup need more than n_ctx {wl.cfg.n_ctx} positions")
 
+    t_open = time.perf_counter()
     m = tp.open_model(path, kv_ctx, rank, world, local) if world > 1 else Model(path, max_ctx=kv_ctx, device=local)
+    open_s = time.perf_counter() - t_open
+    up_s, up_bytes = m.load_stats
     stream = torch.cuda.ExternalStream(m.stream, device=torch.device(f"cuda:{local}"))
 
     # prompt.  One GPU: fwb_prefill (the prompt's tokens through each layer
@@ -480,6 +483,11 @@ def run_b200(args) -> None:
             "clocks": clk,
             "gpu_launches": kernels * K,
         }
+        line["load"] = {"bytes": up_bytes, "upload_s": up_s, "gb_per_s": up_bytes / max(up_s, 1e-9) / 1e9,
+                        "open_s": open_s,
+                        "what": "fwb_model_open: tensor upload from the GGUF mapping (page cache) through pinned "
+                                "staging filled by parallel host threads" + (", this rank's slices" if wl.tp else "")
+                                + "; open_s adds parsing, allocation and the CUDA-graph capture"}
         if prefill:
             line["prefill"] = prefill
         if wl.tp:

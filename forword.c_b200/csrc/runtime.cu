@@ -23,6 +23,7 @@
 #include "gemv.cuh"
 #include "gguf_reader.h"
 #include "tp_shard.h"
+#include "upload.h"
 #include "decode.cuh"
 #include "misc_kernels.cuh"
 #include "gemm_tc.cuh"
@@ -425,6 +426,8 @@ struct fwb_model {
     uint32_t *h_io = nullptr;     // pinned [8]: step in / status out
     float *h_logits = nullptr;    // pinned [n_vocab]
     uint64_t weight_bytes = 0;
+    double load_s = 0;          // time of the tensor upload at open
+    uint64_t load_bytes = 0;    // bytes it moved to the device
     std::vector<fwb::Step> steps;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
@@ -490,20 +493,6 @@ static void free_model(fwb_model *m) {
     if (m->h_logits) cudaFreeHost(m->h_logits);
     if (m->st) cudaStreamDestroy(m->st);
     delete m;
-}
-
-// Upload tensor bytes from the mapping to dst through pinned staging.
-static bool upload(const uint8_t *src, uint8_t *dst, uint64_t bytes, uint8_t *stage[2], cudaEvent_t ev[2],
-                   size_t chunk, cudaStream_t st, int &flip) {
-    for (uint64_t off = 0; off < bytes; off += chunk) {
-        const size_t n = (size_t)std::min<uint64_t>(chunk, bytes - off);
-        CK(cudaEventSynchronize(ev[flip]));
-        std::memcpy(stage[flip], src + off, n);
-        CK(cudaMemcpyAsync(dst + off, stage[flip], n, cudaMemcpyHostToDevice, st));
-        CK(cudaEventRecord(ev[flip], st));
-        flip ^= 1;
-    }
-    return true;
 }
 
 static bool build_steps(fwb_model *m);
@@ -617,41 +606,29 @@ static bool load_model(fwb_model *m, const char *path, size_t max_ctx) {
     const uint64_t arena_bytes = off + 256;
     if (!dalloc(m, (void **)&m->arena, arena_bytes)) return false;
 
-    // upload
+    // upload: every tensor (or this rank's slice of it) into the arena,
+    // staged through pinned buffers by several host threads
     {
-        const size_t chunk = 64u << 20;
-        uint8_t *stage[2] = {nullptr, nullptr};
-        cudaEvent_t ev[2] = {nullptr, nullptr};
-        bool ok = true;
-        if (cudaMallocHost(&stage[0], chunk) != cudaSuccess || cudaMallocHost(&stage[1], chunk) != cudaSuccess ||
-            cudaEventCreateWithFlags(&ev[0], cudaEventDisableTiming) != cudaSuccess ||
-            cudaEventCreateWithFlags(&ev[1], cudaEventDisableTiming) != cudaSuccess) {
-            set_err("pinned staging allocation failed");
-            ok = false;
-        }
-        if (ok) {
-            cudaEventRecord(ev[0], m->st);
-            cudaEventRecord(ev[1], m->st);
-        }
-        int flip = 0;
-        std::vector<uint8_t> shard;
+        Uploader up;
+        bool ok = up.open(m->st);
         for (size_t i = 0; ok && i < plan.size(); ++i) {
             const Pl &e = plan[i];
-            const uint8_t *src = e.t->data;
-            if (e.bytes != e.t->bytes) {  // a slice: packed on the host first
-                shard.resize(e.bytes);
-                tp_extract(*e.t, e.sp, shard.data());
-                src = shard.data();
+            if (e.bytes == e.t->bytes) {
+                const uint8_t *src = e.t->data;
+                ok = up.add(m->arena + e.off, e.bytes,
+                            [src](uint64_t off, uint64_t n, uint8_t *dst) { std::memcpy(dst, src + off, n); });
+            } else {  // a slice: packed straight into the staging buffer
+                const GgufTensor *t = e.t;
+                const ShardSpec sp = e.sp;
+                ok = up.add(m->arena + e.off, e.bytes, [t, sp](uint64_t off, uint64_t n, uint8_t *dst) {
+                    tp_extract_range(*t, sp, off, n, dst);
+                });
             }
-            ok = upload(src, m->arena + e.off, e.bytes, stage, ev, chunk, m->st, flip);
-            if (ok && e.bytes != e.t->bytes && cudaStreamSynchronize(m->st) != cudaSuccess) ok = false;
         }
-        if (ok && cudaStreamSynchronize(m->st) != cudaSuccess) { set_err("upload failed"); ok = false; }
-        for (int i = 0; i < 2; ++i) {
-            if (stage[i]) cudaFreeHost(stage[i]);
-            if (ev[i]) cudaEventDestroy(ev[i]);
-        }
-        if (!ok) return false;
+        if (ok) ok = up.finish();
+        if (!ok) { set_err(up.error().empty() ? "upload failed" : up.error()); return false; }
+        m->load_s = up.seconds();
+        m->load_bytes = up.bytes();
     }
 
     auto mat = [&](const GgufTensor *t, uint64_t o, uint32_t rows, uint32_t cols) {
@@ -1439,6 +1416,13 @@ int fwb_model_dims(const fwb_model_t *m, uint32_t *d) {
 }
 
 uint64_t fwb_model_weight_bytes(const fwb_model_t *m) { return m ? m->weight_bytes : 0; }
+
+int fwb_model_load_stats(const fwb_model_t *m, double *seconds, uint64_t *bytes) {
+    if (!m) return -1;
+    if (seconds) *seconds = m->load_s;
+    if (bytes) *bytes = m->load_bytes;
+    return 0;
+}
 
 int fwb_model_kernels_per_step(const fwb_model_t *m) {
     if (!m) return -1;

@@ -1,6 +1,7 @@
 // tp_shard.cpp — tensor-parallel slices of the llama block (see tp_shard.h).
 #include "tp_shard.h"
 
+#include <algorithm>
 #include <cstring>
 
 namespace fwb {
@@ -63,6 +64,24 @@ void tp_extract(const GgufTensor &t, const ShardSpec &s, uint8_t *dst) {
         return;
     }
     for (uint32_t r = s.r0; r < s.r1; ++r) std::memcpy(dst + (uint64_t)(r - s.r0) * n, t.data + r * row_bytes + off, n);
+}
+
+void tp_extract_range(const GgufTensor &t, const ShardSpec &s, uint64_t off, uint64_t len, uint8_t *dst) {
+    uint32_t v = 1, b = 4;
+    ggml_block(t.type, v, b);
+    const uint64_t row_bytes = t.dims[0] / v * b;
+    const uint64_t c_off = (uint64_t)s.c0 / v * b, n = (uint64_t)(s.c1 - s.c0) / v * b;
+    if (c_off == 0 && n == row_bytes) {  // whole rows: one contiguous range
+        std::memcpy(dst, t.data + (uint64_t)s.r0 * row_bytes + off, len);
+        return;
+    }
+    while (len) {  // packed row r of the slice at r * n
+        const uint64_t r = off / n, in = off % n, take = std::min(len, n - in);
+        std::memcpy(dst, t.data + ((uint64_t)s.r0 + r) * row_bytes + c_off + in, take);
+        dst += take;
+        off += take;
+        len -= take;
+    }
 }
 
 }  // namespace fwb

@@ -36,5 +36,7 @@ ShardSpec tp_shard_spec(const ModelConfig &c, const std::string &name, uint32_t 
 // Bytes of the packed slice, and the copy itself.
 uint64_t tp_shard_bytes(const GgufTensor &t, const ShardSpec &s);
 void tp_extract(const GgufTensor &t, const ShardSpec &s, uint8_t *dst);
+// Bytes [off, off + len) of the packed slice (tp_extract's output) into dst.
+void tp_extract_range(const GgufTensor &t, const ShardSpec &s, uint64_t off, uint64_t len, uint8_t *dst);
 
 }  // namespace fwb

@@ -78,6 +78,14 @@ class Model:
         return int(self.lib.fwb_model_weight_bytes(self.h))
 
     @property
+    def load_stats(self) -> tuple[float, int]:
+        """(seconds, bytes) of the tensor upload at open (fwb_model_load_stats)."""
+        sec = ctypes.c_double()
+        nb = ctypes.c_uint64()
+        self.lib.fwb_model_load_stats(self.h, ctypes.byref(sec), ctypes.byref(nb))
+        return float(sec.value), int(nb.value)
+
+    @property
     def kernels_per_step(self) -> int:
         return int(self.lib.fwb_model_kernels_per_step(self.h))
 

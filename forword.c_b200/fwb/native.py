@@ -88,6 +88,7 @@ def _declare(lib) -> None:
     sig("fwb_trace_cta_read", _i32, _vp, _c.POINTER(_u64), _sz)
     sig("fwb_trace_attn_read", _i32, _vp, _c.POINTER(_u64), _sz)
     sig("fwb_model_weight_bytes", _u64, _vp)
+    sig("fwb_model_load_stats", _i32, _vp, _c.POINTER(_c.c_double), _c.POINTER(_u64))
     sig("fwb_model_kernels_per_step", _i32, _vp)
     sig("fwb_model_open_tp", _vp, _c.c_char_p, _sz, _i32, _i32, _i32)
     sig("fwb_tp_handle", _i32, _vp, _vp)

@@ -160,6 +160,13 @@ int fwb_model_dims(const fwb_model_t *m, uint32_t *dims);
 /* Quantised bytes one decode step streams (weights + norms + one embedding row). */
 uint64_t fwb_model_weight_bytes(const fwb_model_t *m);
 
+/* Time (seconds) and bytes of the tensor upload fwb_model_open did: every
+ * tensor (this rank's slice under tensor parallelism) copied from the GGUF
+ * mapping through pinned staging buffers by parallel host threads, with the
+ * copies to the device overlapped.  No reference counterpart: the reference
+ * reads its mmap on every step (tensor_data.c:25-62). */
+int fwb_model_load_stats(const fwb_model_t *m, double *seconds, uint64_t *bytes);
+
 /* Kernels one decode step launches: 1 for the persistent decode kernel
  * (default), one per phase with FWB_KERNEL_PER_PHASE=1.  -1 for NULL. */
 int fwb_model_kernels_per_step(const fwb_model_t *m);
