@@ -28,6 +28,7 @@
 #include "misc_kernels.cuh"
 #include "gemm_tc.cuh"
 #include "prefill.cuh"
+#include "sampler.cuh"
 
 namespace fwb {
 
@@ -452,6 +453,10 @@ struct fwb_model {
     unsigned long long *attn_trace = nullptr;  // FWB_TRACE: [layer][8] CTA 0's attention item timeline
     // prompt path (fwb_prefill): scratch for kPrefillChunk tokens, allocated
     // at the first call
+    // fwb_sample: scratch of the device sampler, allocated at the first call
+    float *smp_w = nullptr;
+    uint32_t *smp_cnt = nullptr, *smp_hist = nullptr, *smp_out = nullptr, *smp_h_io = nullptr;
+    size_t smp_hist_cap = 0;
     uint32_t pf_cap = 0;
     uint32_t *pf_tok = nullptr;
     float *pf_x = nullptr, *pf_qkv = nullptr, *pf_q = nullptr, *pf_g = nullptr, *pf_u = nullptr;
@@ -490,6 +495,7 @@ static void free_model(fwb_model *m) {
     if (m->graph) cudaGraphDestroy(m->graph);
     for (void *p : m->allocs) cudaFree(p);
     if (m->h_io) cudaFreeHost(m->h_io);
+    if (m->smp_h_io) cudaFreeHost(m->smp_h_io);
     if (m->h_logits) cudaFreeHost(m->h_logits);
     if (m->st) cudaStreamDestroy(m->st);
     delete m;
@@ -1694,6 +1700,76 @@ int fwb_trace_attn_read(fwb_model_t *m, uint64_t *out, size_t n) {
 }
 
 void *fwb_stream(fwb_model_t *m) { return m ? (void *)m->st : nullptr; }
+
+// xorshift64 of sampler.c:8-10 and the uniform draw of sampler.c:93
+static float sample_uniform(uint64_t *s) {
+    uint64_t x = *s;
+    x ^= x << 13;
+    x ^= x >> 7;
+    x ^= x << 17;
+    *s = x;
+    return (float)(x >> 11) / (float)(UINT64_MAX >> 11);
+}
+
+int fwb_sample(fwb_model_t *m, const uint32_t *history, size_t n_history, float temperature, float top_p,
+               float rep_penalty, uint64_t *rng_state, uint32_t *next_token) {
+    if (!m || !next_token || (n_history && !history) || (temperature > 0.0f && !rng_state)) {
+        set_err("fwb_sample: null argument");
+        return -1;
+    }
+    if (m->world > 1 && !m->connected) { set_err("fwb_sample: tensor parallel model not connected"); return -1; }
+    cudaSetDevice(m->dev);
+    const uint32_t n = m->cfg.n_vocab;
+    static bool attr_set[64] = {};
+    if (m->dev < 64 && !attr_set[m->dev]) {
+        if (cudaFuncSetAttribute((const void *)sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kSampleDynSmem) != cudaSuccess) {
+            set_err("fwb_sample: shared memory attribute");
+            return -1;
+        }
+        attr_set[m->dev] = true;
+    }
+    if (!m->smp_w) {
+        if (!dalloc(m, (void **)&m->smp_w, (size_t)n * 4) || !dalloc(m, (void **)&m->smp_cnt, (size_t)n * 4) ||
+            !dalloc(m, (void **)&m->smp_out, 64))
+            return -1;
+        if (cudaMallocHost(&m->smp_h_io, 64) != cudaSuccess) { set_err("fwb_sample: pinned buffer"); return -1; }
+    }
+    if (n_history > m->smp_hist_cap) {
+        const size_t cap = std::max<size_t>(n_history, 2 * (size_t)m->kv_ctx);
+        if (!dalloc(m, (void **)&m->smp_hist, cap * 4)) return -1;
+        m->smp_hist_cap = cap;
+    }
+    SampleArgs a{};
+    a.n = n;
+    a.world = m->world;
+    a.slice = n / m->world;
+    if (m->world == 1) a.lg[0] = m->logits;
+    else
+        for (uint32_t q = 0; q < m->world; ++q) a.lg[q] = reinterpret_cast<const float *>(m->peer[q] + m->x_logits);
+    a.w = m->smp_w;
+    a.cnt = m->smp_cnt;
+    a.hist = m->smp_hist;
+    a.n_hist = (uint32_t)n_history;
+    a.temp = temperature;
+    a.top_p = top_p;
+    a.pen = rep_penalty;
+    a.u = temperature > 0.0f ? sample_uniform(rng_state) : 0.0f;
+    a.out = m->smp_out;
+    if (n_history && cudaMemcpyAsync(m->smp_hist, history, n_history * 4, cudaMemcpyHostToDevice, m->st) != cudaSuccess) {
+        set_err("fwb_sample: history copy failed");
+        return -1;
+    }
+    sample_kernel<<<1, kSampleThreads, kSampleDynSmem, m->st>>>(a);
+    if (cudaGetLastError() != cudaSuccess ||
+        cudaMemcpyAsync(m->smp_h_io, m->smp_out, 4, cudaMemcpyDeviceToHost, m->st) != cudaSuccess ||
+        cudaStreamSynchronize(m->st) != cudaSuccess) {
+        set_err("fwb_sample: kernel failed");
+        return -1;
+    }
+    *next_token = m->smp_h_io[0];
+    return 0;
+}
 
 void *fwb_host_alloc(size_t bytes) {
     void *p = nullptr;

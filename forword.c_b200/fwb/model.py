@@ -130,6 +130,18 @@ class Model:
             raise FwbError(f"fwb_generate_greedy: {_err(self.lib)}")
         return out
 
+    def sample(self, history, temperature: float, top_p: float, rep_penalty: float,
+               rng_state: int) -> tuple[int, int]:
+        """fwb_sample on the last step's device logits: (token, new rng state)."""
+        h = np.ascontiguousarray(history, dtype=np.uint32)
+        st = ctypes.c_uint64(rng_state)
+        tok = ctypes.c_uint32()
+        rc = self.lib.fwb_sample(self.h, h.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)), h.size, temperature,
+                                 top_p, rep_penalty, ctypes.byref(st), ctypes.byref(tok))
+        if rc != 0:
+            raise FwbError(f"fwb_sample: {_err(self.lib)}")
+        return int(tok.value), int(st.value)
+
     def kv_load(self, layer: int, pos0: int, k: np.ndarray, v: np.ndarray) -> None:
         k = np.ascontiguousarray(k, dtype=np.float32)
         v = np.ascontiguousarray(v, dtype=np.float32)

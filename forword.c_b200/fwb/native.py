@@ -82,6 +82,8 @@ def _declare(lib) -> None:
     sig("fwb_kv_read", _i32, _vp, _sz, _sz, _sz, _fp, _fp)
     sig("fwb_generate_greedy", _i32, _vp, _u32, _sz, _sz, _c.POINTER(_u32))
     sig("fwb_logits_dev", _vp, _vp)
+    sig("fwb_sample", _i32, _vp, _c.POINTER(_u32), _sz, _c.c_float, _c.c_float, _c.c_float,
+        _c.POINTER(_u64), _c.POINTER(_u32))
     sig("fwb_stream", _vp, _vp)
     sig("fwb_trace_read", _i32, _vp, _c.POINTER(_u64), _sz, _c.c_char_p, _sz)
     sig("fwb_prof_read", _i32, _vp, _c.POINTER(_u64), _sz)

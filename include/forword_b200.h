@@ -209,6 +209,25 @@ int fwb_generate_greedy(fwb_model_t *m, uint32_t first_token, size_t pos0, size_
                         uint32_t *tokens_out);
 
 /*
+ * Sample the next token from the logits of the last step without copying
+ * them to the host: main.c:176-188 with sampler.c, on the device.  The
+ * repetition penalty (sampler_rep_penalty, sampler.c:86-100) is applied for
+ * every entry of history[0..n_history) (prompt and generated tokens, as
+ * main.c keeps them); then temperature <= 0 gives the greedy argmax
+ * (sampler_argmax), otherwise temperature, softmax and top-p sampling
+ * (sampler_top_p, sampler.c:46-84) with one draw of the reference's
+ * xorshift64 generator, whose state *rng_state advances exactly as the
+ * reference's does (only when temperature > 0).  The nucleus and the draw
+ * are found by radix selection with fixed-point sums instead of a sort of
+ * the vocabulary; the token can differ from the reference's only where the
+ * draw or top_p falls within about 1e-7 of a cumulative probability
+ * boundary.  Under tensor parallelism every rank makes the same call (the
+ * other ranks' logits are read over NVLink).  Synchronous.
+ */
+int fwb_sample(fwb_model_t *m, const uint32_t *history, size_t n_history, float temperature, float top_p,
+               float rep_penalty, uint64_t *rng_state, uint32_t *next_token);
+
+/*
  * Write (load) or read K/V of n positions [pos0, pos0+n) of one layer.
  * k and v are host fp32 arrays [n][n_head_kv][head_dim] — the reference's
  * kv_cache row order (kv_cache.h:13,45-51).

@@ -1,0 +1,161 @@
+"""fwb_sample (the reference's sampling on the device logits) against the
+reference's own sampler.c, compiled from its sources (oracle/_ref).
+
+* Identical inputs: the device logits of a decode step are copied to the
+  host and given to the reference's sampler_rep_penalty + sampler_top_p /
+  sampler_argmax with the same history and xorshift state; fwb_sample on the
+  same device logits must pick the same token and leave the same generator
+  state, over many (temperature, top_p, penalty, seed) combinations.  The
+  device sums probabilities in fixed point instead of the reference's fp32
+  running sums, so a different token is accepted only where the
+  reference's own draw lies within 1e-5 (relative) of a cumulative
+  boundary; the test reports how close the nearest case came.
+* A sampled generation loop written like main.c:173-218 (history = prompt +
+  generated tokens, rep-pen 1.1, temperature 0.8, top-p 0.9, seeded) gives
+  the same token stream with fwb_sample on the GPU model as with the
+  compiled reference's transformer_forward and sampler on the CPU.
+* The forword.c CLI linked through the shim (host sampler on the library's
+  logits) prints the same text as the reference CLI for a seeded
+  non-greedy run.
+"""
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+import pytest
+
+import pyoracle
+from fwb import configs, gguf_synth, native
+from fwb.model import Model
+
+pytestmark = pytest.mark.gpu
+_fp = ctypes.POINTER(ctypes.c_float)
+_u32p = ctypes.POINTER(ctypes.c_uint32)
+
+
+@pytest.fixture(scope="module")
+def ref_sampler(built):
+    if native.product().fwb_device_count() < 1:
+        pytest.skip("no CUDA device")
+    if not pyoracle.ref_available():
+        pytest.skip("compiled reference not built")
+    lib = pyoracle.ref_lib()
+    lib.sampler_rep_penalty.argtypes = [_fp, ctypes.c_size_t, _u32p, ctypes.c_size_t, ctypes.c_float]
+    lib.sampler_rep_penalty.restype = None
+    lib.sampler_top_p.argtypes = [_fp, ctypes.c_size_t, ctypes.c_float, ctypes.c_float,
+                                  ctypes.POINTER(ctypes.c_uint64)]
+    lib.sampler_top_p.restype = ctypes.c_uint32
+    lib.sampler_argmax.argtypes = [_fp, ctypes.c_size_t]
+    lib.sampler_argmax.restype = ctypes.c_uint32
+    return lib
+
+
+def ref_sample(lib, logits, history, temp, top_p, pen, state):
+    """main.c:176-188 with the reference's sampler: (token, new state)."""
+    lg = np.array(logits, dtype=np.float32, copy=True)
+    h = np.ascontiguousarray(history, dtype=np.uint32)
+    lib.sampler_rep_penalty(lg.ctypes.data_as(_fp), lg.size, h.ctypes.data_as(_u32p), h.size, pen)
+    if temp <= 0:
+        return int(lib.sampler_argmax(lg.ctypes.data_as(_fp), lg.size)), state
+    st = ctypes.c_uint64(state)
+    tok = int(lib.sampler_top_p(lg.ctypes.data_as(_fp), lg.size, temp, top_p, ctypes.byref(st)))
+    return tok, int(st.value)
+
+
+def boundary_margin(logits, history, temp, top_p, pen, state) -> float:
+    """Relative distance of the reference's draw from the nearest cumulative
+    boundary of its sorted nucleus (float64 emulation of sampler.c)."""
+    lg = np.array(logits, dtype=np.float64)
+    for t in history:
+        lg[t] = lg[t] / pen if lg[t] > 0 else lg[t] * pen
+    lg /= temp
+    p = np.exp(lg - lg.max())
+    p /= p.sum()
+    order = np.lexsort((np.arange(p.size), -p))
+    c = np.cumsum(p[order])
+    nuc = int(np.searchsorted(c, top_p) + 1)
+    norm = c[nuc - 1]
+    x = state
+    x ^= (x << 13) & (2**64 - 1)
+    x ^= x >> 7
+    x ^= (x << 17) & (2**64 - 1)
+    r = (x >> 11) / float(2**53 - 1) * norm
+    return float(np.min(np.abs(c[:nuc] - r)) / norm)
+
+
+def test_device_sampler_matches_reference_sampler(ref_sampler, model_dir):
+    cfg = configs.SMALL_Q4_0
+    path = gguf_synth.write_model(os.path.join(model_dir, "sampler.gguf"), cfg, seed=61)
+    rng = np.random.default_rng(5)
+    close = []
+    with Model(path) as m:
+        tok = 3
+        history = [3]
+        n_checked = 0
+        for pos in range(24):
+            logits = m.forward(tok, pos)
+            for temp, top_p, pen in ((0.8, 0.9, 1.1), (1.0, 0.95, 1.0), (0.5, 0.5, 1.3), (1.3, 1.0, 1.1),
+                                     (0.0, 0.9, 1.1), (0.7, 0.2, 1.0)):
+                seed = int(rng.integers(1, 2**63))
+                want, st_ref = ref_sample(ref_sampler, logits, history, temp, top_p, pen, seed)
+                got, st_dev = m.sample(history, temp, top_p, pen, seed)
+                assert st_dev == st_ref, "generator state advanced differently"
+                if got != want:
+                    margin = boundary_margin(logits, history, temp, top_p, pen, seed) if temp > 0 else 0.0
+                    assert temp > 0 and margin < 1e-5, (
+                        f"pos {pos} temp {temp} top_p {top_p} pen {pen}: device {got}, reference {want} "
+                        f"(draw {margin:.2e} from a boundary)")
+                    close.append(margin)
+                n_checked += 1
+            tok = int(rng.integers(0, cfg.n_vocab))
+            history.append(tok)
+    print(f"{n_checked} draws; {len(close)} differed, all within 1e-5 of a boundary")
+
+
+def test_sampled_generation_loop_matches_reference(ref_sampler, model_dir):
+    """main.c's generation loop (history, rep-pen, temperature, top-p, one
+    seeded generator) on the GPU model with fwb_sample, against the same
+    loop on the compiled reference (transformer_forward + sampler.c)."""
+    cfg = configs.TINY
+    path = gguf_synth.write_model(os.path.join(model_dir, "sampler_loop.gguf"), cfg, seed=62)
+    prompt = [1, 300, 301, 302, 303, 310]
+    temp, top_p, pen, seed, n_gen = 0.8, 0.9, 1.1, 42, 48
+
+    def run(forward, pick):
+        history = list(prompt)
+        state = seed
+        for i, t in enumerate(prompt[:-1]):
+            forward(t, i)
+        logits = forward(prompt[-1], len(prompt) - 1)
+        out = []
+        for g in range(n_gen):
+            tok, state = pick(logits, history, state)
+            out.append(tok)
+            history.append(tok)
+            logits = forward(tok, len(prompt) + g)
+        return out
+
+    ref = pyoracle.RefModel(path, 0)
+    want = run(ref.forward, lambda lg, h, s: ref_sample(ref_sampler, lg, h, temp, top_p, pen, s))
+    ref.close()
+    with Model(path) as m:
+        got = run(m.forward, lambda lg, h, s: m.sample(h, temp, top_p, pen, s))
+    assert got == want, f"sampled streams differ: {got} vs {want}"
+
+
+B200_CLI = os.path.join(native.PKG_DIR, "_build", "forword-b200")
+
+
+def test_cli_sampled_output_identical(ref_sampler, model_dir):
+    for exe in (B200_CLI, pyoracle.REF_CLI):
+        if not os.path.exists(exe):
+            pytest.skip(f"CLI not built: {exe}")
+    cfg = configs.TINY
+    path = gguf_synth.write_model(os.path.join(model_dir, "cli_sampled.gguf"), cfg, seed=63)
+    args = [path, "--temp", "0.8", "--top-p", "0.9", "--rep-pen", "1.1", "--seed", "42", "--no-template",
+            "--max-tokens", "48", "--ctx", "128", "t1 t2 t3 t17 t99"]
+    outs = [subprocess.run([exe] + args, capture_output=True, text=True, timeout=600) for exe in (B200_CLI, pyoracle.REF_CLI)]
+    assert outs[1].returncode == 0, outs[1].stderr
+    assert outs[0].returncode == 0, outs[0].stderr
+    assert outs[0].stdout == outs[1].stdout
