@@ -191,14 +191,14 @@ _CLOCK_FIELDS = ("timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reas
 
 
 class ClockSampler:
-    """nvidia-smi sampled every 100 ms for one device (read-only queries)."""
+    """nvidia-smi sampled every 20 ms for one device (read-only queries)."""
 
     def __init__(self, device: int):
         self.proc = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(device), f"--query-gpu={_CLOCK_FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None

@@ -113,35 +113,70 @@ def test_device_sampler_matches_reference_sampler(ref_sampler, model_dir):
     print(f"{n_checked} draws; {len(close)} differed, all within 1e-5 of a boundary")
 
 
+def cum_shift_explains(lg_gpu, lg_ref, history, temp, top_p, pen, state) -> tuple[bool, float, float]:
+    """Whether the draw's distance to its nearest cumulative boundary (on the
+    reference's logits) is within the shift that the two models' logit
+    differences cause in the sorted running sums: (explained, margin, shift)."""
+    def probs(lg):
+        x = np.array(lg, dtype=np.float64)
+        for t in history:
+            x[t] = x[t] / pen if x[t] > 0 else x[t] * pen
+        x /= temp
+        p = np.exp(x - x.max())
+        return p / p.sum()
+    p_r, p_g = probs(lg_ref), probs(lg_gpu)
+    order = np.lexsort((np.arange(p_r.size), -p_r))
+    c_r, c_g = np.cumsum(p_r[order]), np.cumsum(p_g[order])
+    nuc = int(np.searchsorted(c_r, top_p) + 1)
+    x = state
+    x ^= (x << 13) & (2**64 - 1)
+    x ^= x >> 7
+    x ^= (x << 17) & (2**64 - 1)
+    r = (x >> 11) / float(2**53 - 1) * c_r[nuc - 1]
+    margin = float(np.min(np.abs(c_r[:nuc] - r)))
+    shift = float(np.max(np.abs(c_g[:nuc] - c_r[:nuc])))
+    return margin <= 2 * shift + 1e-7, margin, shift
+
+
 def test_sampled_generation_loop_matches_reference(ref_sampler, model_dir):
     """main.c's generation loop (history, rep-pen, temperature, top-p, one
-    seeded generator) on the GPU model with fwb_sample, against the same
-    loop on the compiled reference (transformer_forward + sampler.c)."""
+    seeded generator) with fwb_sample on the GPU model, against the same
+    loop with the compiled reference's transformer_forward and sampler.c,
+    teacher-forced on the reference's tokens.  The two models' logits agree
+    to ~1e-5, not bit for bit, and over a flat distribution (thousands of
+    tokens in the nucleus of this random-weight model) that moves the
+    running sums by more than some tokens' probabilities: a step may pick a
+    different token only where the reference's draw lies within that shift
+    of a boundary, and most steps must agree."""
     cfg = configs.TINY
     path = gguf_synth.write_model(os.path.join(model_dir, "sampler_loop.gguf"), cfg, seed=62)
     prompt = [1, 300, 301, 302, 303, 310]
     temp, top_p, pen, seed, n_gen = 0.8, 0.9, 1.1, 42, 48
-
-    def run(forward, pick):
-        history = list(prompt)
-        state = seed
-        for i, t in enumerate(prompt[:-1]):
-            forward(t, i)
-        logits = forward(prompt[-1], len(prompt) - 1)
-        out = []
-        for g in range(n_gen):
-            tok, state = pick(logits, history, state)
-            out.append(tok)
-            history.append(tok)
-            logits = forward(tok, len(prompt) + g)
-        return out
-
     ref = pyoracle.RefModel(path, 0)
-    want = run(ref.forward, lambda lg, h, s: ref_sample(ref_sampler, lg, h, temp, top_p, pen, s))
-    ref.close()
     with Model(path) as m:
-        got = run(m.forward, lambda lg, h, s: m.sample(h, temp, top_p, pen, s))
-    assert got == want, f"sampled streams differ: {got} vs {want}"
+        for i, t in enumerate(prompt[:-1]):
+            ref.forward(t, i)
+            m.forward(t, i)
+        history, state, tok = list(prompt), seed, prompt[-1]
+        same, diffs = 0, []
+        for g in range(n_gen):
+            pos = len(prompt) - 1 + g
+            lg_r, lg_g = ref.forward(tok, pos), m.forward(tok, pos)
+            want, st_r = ref_sample(ref_sampler, lg_r, history, temp, top_p, pen, state)
+            got, st_g = m.sample(history, temp, top_p, pen, state)
+            assert st_g == st_r
+            if got == want:
+                same += 1
+            else:
+                ok, margin, shift = cum_shift_explains(lg_g, lg_r, history, temp, top_p, pen, state)
+                assert ok, f"step {g}: device {got}, reference {want}; draw {margin:.2e} from a boundary, " \
+                           f"logit-induced shift only {shift:.2e}"
+                diffs.append((g, margin, shift))
+            state, tok = st_r, want
+            history.append(want)
+    ref.close()
+    print(f"{same}/{n_gen} sampled tokens identical; differing steps (step, margin, shift): {diffs}")
+    assert same >= n_gen * 3 // 4
 
 
 B200_CLI = os.path.join(native.PKG_DIR, "_build", "forword-b200")
