@@ -445,6 +445,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel_t(const __gri
                     case QT_Q4_0: r = gemv_phase_q<QT_Q4_0, HALF>(P, sm, rs, tab, d.n_ph, total, d.NS, d.stage_bytes, pos); break;
                     case QT_Q5_0: r = gemv_phase_q<QT_Q5_0, HALF>(P, sm, rs, tab, d.n_ph, total, d.NS, d.stage_bytes, pos); break;
                     case QT_Q8_0: r = gemv_phase_q<QT_Q8_0, HALF>(P, sm, rs, tab, d.n_ph, total, d.NS, d.stage_bytes, pos); break;
+                    case QT_Q5_1: r = gemv_phase_t<QT_Q5_1, true, HALF>(&P.g, sm, rs, tab, d.n_ph, total, d.NS, d.stage_bytes, pos); break;
+                    case QT_Q4_K: r = gemv_phase_t<QT_Q4_K, true, HALF>(&P.g, sm, rs, tab, d.n_ph, total, d.NS, d.stage_bytes, pos); break;
+                    case QT_Q6_K: r = gemv_phase_t<QT_Q6_K, true, HALF>(&P.g, sm, rs, tab, d.n_ph, total, d.NS, d.stage_bytes, pos); break;
                     default: break;
                     }
                 }
@@ -461,10 +464,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel_t(const __gri
                 const EmbedArgs &e = P.e;
                 const uint32_t tok = __ldcg(&e.step[0]);
                 const uint8_t *row = e.table + (uint64_t)tok * e.row_bytes;
-                const uint32_t bb = e.type == 2 ? 18 : e.type == 6 ? 22 : 34;
                 for (uint32_t i = blockIdx.x * blockDim.x + tid; i < e.cols; i += gridDim.x * blockDim.x)
-                    e.x[i] = e.type == 0 ? reinterpret_cast<const float *>(row)[i]
-                                         : decode_value(row + (i >> 5) * bb, e.type, i & 31);
+                    e.x[i] = e.type == 0 ? reinterpret_cast<const float *>(row)[i] : decode_elem(row, e.type, i);
             }
         } else if (P.kind == PH_GEMV) {
             // aborted: still walk the ring so that every issued stage is

@@ -50,20 +50,33 @@
 
 namespace fwb {
 
-enum QType : int { QT_Q4_0 = 2, QT_Q5_0 = 6, QT_Q8_0 = 8 };
+enum QType : int { QT_Q4_0 = 2, QT_Q5_0 = 6, QT_Q5_1 = 7, QT_Q8_0 = 8, QT_Q4_K = 12, QT_Q6_K = 14 };
 template <int QT> struct QTraits;
-// BB block bytes, OFF quant offset, RPT rows per thread per round: four
+// BB block bytes (superblock bytes for the K-quants), OFF quant offset folded
+// into the accumulator starts, RPT rows per thread per round: four
 // independent rows (the per-round ring wait, release and reduction are paid
 // once per four rows; measured 5 % faster per decode step than two), two for
-// Q8_0, whose 34-byte blocks need more registers per row
-template <> struct QTraits<QT_Q4_0> { static constexpr int BB = 18, OFF = 8, RPT = 4; };
-template <> struct QTraits<QT_Q5_0> { static constexpr int BB = 22, OFF = 16, RPT = 4; };
-template <> struct QTraits<QT_Q8_0> { static constexpr int BB = 34, OFF = 0, RPT = 2; };
+// the types whose units need more registers.  SUMX: the block dot needs the
+// block's sum of inputs (a min term: Q5_1 d*q + m, Q4_K d*sc*q - dmin*m).
+// SUPER: 256-value superblocks, a thread's 64-value unit is a quarter of one.
+template <> struct QTraits<QT_Q4_0> { static constexpr int BB = 18, OFF = 8, RPT = 4; static constexpr bool SUMX = false, SUPER = false; };
+template <> struct QTraits<QT_Q5_0> { static constexpr int BB = 22, OFF = 16, RPT = 4; static constexpr bool SUMX = false, SUPER = false; };
+template <> struct QTraits<QT_Q5_1> { static constexpr int BB = 24, OFF = 0, RPT = 2; static constexpr bool SUMX = true, SUPER = false; };
+template <> struct QTraits<QT_Q8_0> { static constexpr int BB = 34, OFF = 0, RPT = 2; static constexpr bool SUMX = false, SUPER = false; };
+template <> struct QTraits<QT_Q4_K> { static constexpr int BB = 144, OFF = 0, RPT = 2; static constexpr bool SUMX = true, SUPER = true; };
+template <> struct QTraits<QT_Q6_K> { static constexpr int BB = 210, OFF = 0, RPT = 2; static constexpr bool SUMX = false, SUPER = true; };
 
-// half: the halved row count (2, 1 for Q8_0) that the persistent kernel uses
-// when the ring of four-row stages does not fit its shared memory
+// half: the halved row count (2, 1 for two-row types) that the persistent
+// kernel uses when the ring of full stages does not fit its shared memory
 __host__ __device__ constexpr uint32_t rows_per_thread(int qt, bool half = false) {
-    return (qt == QT_Q8_0 ? 2u : 4u) >> (half ? 1 : 0);
+    return (qt == QT_Q4_0 || qt == QT_Q5_0 ? 4u : 2u) >> (half ? 1 : 0);
+}
+
+// Byte offset of unit u (values [64u, 64u + 64)) within a row; for the
+// K-quants the start of its superblock.
+template <int QT>
+__host__ __device__ constexpr uint32_t unit_bytes(uint32_t u) {
+    return QTraits<QT>::SUPER ? (u >> 2) * (uint32_t)QTraits<QT>::BB : u * 2u * (uint32_t)QTraits<QT>::BB;
 }
 
 enum GemvMode : int {
@@ -140,7 +153,8 @@ __device__ __forceinline__ unsigned long long gtime_ns() {
 // ---------------------------------------------------------------------------
 struct XBlock {
     uint32_t hi[8], mid[8], lo[8];  // 4 elements per word, element order 4k..4k+3
-    int ih, im, il;                 // accumulator starts: kMagicBits - OFF * (sum of the plane's digits)
+    int ih, im, il;                 // accumulator starts: kMagicBits - OFF * (sum of the plane's digits);
+                                    // SUMX types: ih holds the float bits of sum(X), im = il = kMagicBits
     float s;                        // s_b
 };
 
@@ -212,6 +226,118 @@ __device__ __forceinline__ float block_scale(uint32_t dbits, const XBlock &x) {
     return f16_bits_to_f32(dbits) * x.s;
 }
 
+// the three plane dots of 4 quant bytes with input word k: unsigned and
+// signed quants
+__device__ __forceinline__ void acc3_u(uint32_t q, const XBlock &x, int k, int &A, int &M, int &B) {
+    A = dp4a_us(q, (int)x.hi[k], A);
+    M = dp4a_uu(q, x.mid[k], M);
+    B = dp4a_uu(q, x.lo[k], B);
+}
+__device__ __forceinline__ void acc3_s(uint32_t q, const XBlock &x, int k, int &A, int &M, int &B) {
+    A = dp4a_ss((int)q, (int)x.hi[k], A);
+    M = dp4a_su((int)q, x.mid[k], M);
+    B = dp4a_su((int)q, x.lo[k], B);
+}
+
+// Q5_1 block (6 words: d | m << 16, qh, 4 nibble words): s * (d * sum(q X) + m * sum(X))
+__device__ __forceinline__ float dot_q5_1(const uint32_t *w, const XBlock &x) {
+    int A = kMagicBits, M = kMagicBits, B = kMagicBits;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        acc3_u((w[2 + k] & 0x0F0F0F0Fu) | spread4(w[1] >> (4 * k)), x, k, A, M, B);
+        acc3_u(((w[2 + k] >> 4) & 0x0F0F0F0Fu) | spread4(w[1] >> (16 + 4 * k)), x, k + 4, A, M, B);
+    }
+    const float T = finish_block(A, M, B);
+    return x.s * fmaf(f16_bits_to_f32(w[0]), T, f16_bits_to_f32(w[0] >> 16) * __int_as_float(x.ih));
+}
+
+// Q4_K 6-bit scale and min of group g from the 12 scale bytes (words y, z,
+// w of the superblock's header): get_scale_min_k4, quant.c:63-82
+__device__ __forceinline__ void k4_scale_min(const uint4 &h, uint32_t g, float &sc, float &mn) {
+    auto byte = [&](uint32_t i) -> uint32_t {
+        const uint32_t wv = i < 4 ? h.y : (i < 8 ? h.z : h.w);
+        return (wv >> (8 * (i & 3))) & 0xffu;
+    };
+    uint32_t a, b;
+    if (g < 4) {
+        a = byte(g) & 63u;
+        b = byte(g + 4) & 63u;
+    } else {
+        a = (byte(g + 4) & 15u) | ((byte(g - 4) >> 6) << 4);
+        b = (byte(g + 4) >> 4) | ((byte(g) >> 6) << 4);
+    }
+    sc = (float)a;
+    mn = (float)b;
+}
+
+// Q4_K unit sub of a superblock (16-byte aligned): groups 2 sub (low nibbles
+// of the 32 quant bytes, block a) and 2 sub + 1 (high nibbles, block b);
+// block dot = s * (d * sc * sum(q X) - dmin * m * sum(X))
+__device__ __forceinline__ float dot_q4_k_unit(const uint8_t *sb, uint32_t sub, const XBlock &xa,
+                                               const XBlock &xb) {
+    const uint4 h = *reinterpret_cast<const uint4 *>(sb);
+    const uint4 qa = *reinterpret_cast<const uint4 *>(sb + 16 + 32 * sub);
+    const uint4 qb = *reinterpret_cast<const uint4 *>(sb + 32 + 32 * sub);
+    const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+    int A = kMagicBits, M = kMagicBits, B = kMagicBits;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc3_u(q[k] & 0x0F0F0F0Fu, xa, k, A, M, B);
+    const float Ta = finish_block(A, M, B);
+    A = M = B = kMagicBits;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc3_u((q[k] >> 4) & 0x0F0F0F0Fu, xb, k, A, M, B);
+    const float Tb = finish_block(A, M, B);
+    const float d = f16_bits_to_f32(h.x), dmin = f16_bits_to_f32(h.x >> 16);
+    float sa, ma, sb_, mb;
+    k4_scale_min(h, 2 * sub, sa, ma);
+    k4_scale_min(h, 2 * sub + 1, sb_, mb);
+    const float va = xa.s * fmaf(d * sa, Ta, -(dmin * ma) * __int_as_float(xa.ih));
+    return fmaf(xb.s, fmaf(d * sb_, Tb, -(dmin * mb) * __int_as_float(xb.ih)), va);
+}
+
+// Q6_K: 6-bit quants as signed bytes q - 32 (byte-wise: set bit 7, subtract
+// 32, flip bit 7; no borrow crosses a byte since every byte is >= 128 + 0)
+__device__ __forceinline__ uint32_t q6_signed(uint32_t low4, uint32_t high2) {
+    return (((low4 | (high2 << 4)) | 0x80808080u) - 0x20202020u) ^ 0x80808080u;
+}
+
+template <int NWORDS, bool A4>
+__device__ __forceinline__ void load_unit_words(const uint8_t *p, uint32_t (&w)[NWORDS]);
+
+// Q6_K unit sub of a superblock at sb (2-byte aligned): half = sub / 2 of
+// the superblock, its values [0, 32) + 64 * (sub & 1) (block a: low/high
+// nibbles of ql[0..32) by sub & 1, high bits qh bits 0-1 / 4-5) and
+// [32, 64) + 64 * (sub & 1) (block b: ql[32..64), qh bits 2-3 / 6-7), with an
+// int8 scale per 16 values: block dot = s * d * sum_halves sc * sum((q - 32) X)
+__device__ __forceinline__ float dot_q6_k_unit(const uint8_t *sb, uint32_t sub, const XBlock &xa,
+                                               const XBlock &xb) {
+    const uint32_t half = sub >> 1, sl = 4 * (sub & 1);
+    uint32_t qh[8], scw[1], dw[1];
+    load_unit_words<8, false>(sb + 128 + 32 * half, qh);
+    load_unit_words<1, false>(sb + 192 + 8 * half + 4 * (sub & 1), scw);
+    load_unit_words<1, false>(sb + 208, dw);
+    const float d = f16_bits_to_f32(dw[0]);
+    float v[2];
+#pragma unroll
+    for (int blk = 0; blk < 2; ++blk) {
+        const XBlock &x = blk ? xb : xa;
+        uint32_t ql[8];
+        load_unit_words<8, false>(sb + 64 * half + 32 * blk, ql);
+        float T[2];
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+            int A = kMagicBits, M = kMagicBits, B = kMagicBits;
+#pragma unroll
+            for (int k = 4 * hh; k < 4 * hh + 4; ++k)
+                acc3_s(q6_signed((ql[k] >> sl) & 0x0F0F0F0Fu, (qh[k] >> (sl + 2 * blk)) & 0x03030303u), x, k, A, M, B);
+            T[hh] = finish_block(A, M, B);
+        }
+        const float s0 = (float)(int8_t)(scw[0] >> (16 * blk)), s1 = (float)(int8_t)(scw[0] >> (16 * blk + 8));
+        v[blk] = x.s * fmaf(s0, T[0], s1 * T[1]);
+    }
+    return d * (v[0] + v[1]);
+}
+
 // Words of one unit (two blocks, 2*BB bytes) starting at p (2-byte aligned;
 // 4-byte aligned when A4).
 template <int NWORDS, bool A4>
@@ -236,8 +362,19 @@ __device__ __forceinline__ void load_unit_words(const uint8_t *p, uint32_t (&w)[
 // way and selected, so the row loop has no divergent branch; the bytes read
 // past the end of a row with an odd block count stay inside the stage slack).
 template <int QT, bool A4>
-__device__ __forceinline__ float unit_dot(const uint8_t *p, const XBlock &xa, const XBlock &xb, bool two) {
-    if constexpr (QT == QT_Q4_0) {
+__device__ __forceinline__ float unit_dot(const uint8_t *p, const XBlock &xa, const XBlock &xb, bool two,
+                                          uint32_t sub) {
+    if constexpr (QT == QT_Q4_K) {
+        return dot_q4_k_unit(p, sub, xa, xb);
+    } else if constexpr (QT == QT_Q6_K) {
+        return dot_q6_k_unit(p, sub, xa, xb);
+    } else if constexpr (QT == QT_Q5_1) {
+        uint32_t w[12];
+        load_unit_words<12, true>(p, w);
+        const float r = dot_q5_1(w, xa);
+        const float r2 = dot_q5_1(w + 6, xb);
+        return two ? r + r2 : r;
+    } else if constexpr (QT == QT_Q4_0) {
         uint32_t w[9];
         load_unit_words<9, A4>(p, w);
         uint32_t qa[4] = {__funnelshift_r(w[0], w[1], 16), __funnelshift_r(w[1], w[2], 16),
@@ -431,10 +568,11 @@ __device__ __forceinline__ void ring_advance(RingState &rs, uint32_t NS) {
 // are issued before any is used, and the passes have no early exit, so their
 // dependency chains (block maximum, shuffles, rounding) overlap.  Blocks at
 // or beyond nb are predicated off.
-template <int OFF, int NP>
+template <int QT, int NP>
 __device__ __forceinline__ void plane_passes(const GemvArgs &a, const GemvSmem &sm, uint32_t tid, uint32_t b0,
                                              uint32_t per, bool norm, float &ss, bool prof,
                                              unsigned long long &t_x) {
+    constexpr int OFF = QTraits<QT>::OFF;
     const uint32_t nb = a.K >> 5, nbp = sm.nbp;
     const uint32_t q = tid & 3;
     {
@@ -522,9 +660,15 @@ __device__ __forceinline__ void plane_passes(const GemvArgs &a, const GemvSmem &
                     sm.planes[(2 * 8 + k) * nbp + b] = pw[2][w];
                 }
                 if (q == 0) {
-                    sm.planes[24 * nbp + b] = (uint32_t)(kMagicBits - OFF * sh);
-                    sm.planes[25 * nbp + b] = (uint32_t)(kMagicBits - OFF * sm_);
-                    sm.planes[26 * nbp + b] = (uint32_t)(kMagicBits - OFF * sl);
+                    if constexpr (QTraits<QT>::SUMX) {  // sum(X) for the min term, exact in int32
+                        sm.planes[24 * nbp + b] = __float_as_uint((float)(65536 * sh + 256 * sm_ + sl));
+                        sm.planes[25 * nbp + b] = (uint32_t)kMagicBits;
+                        sm.planes[26 * nbp + b] = (uint32_t)kMagicBits;
+                    } else {
+                        sm.planes[24 * nbp + b] = (uint32_t)(kMagicBits - OFF * sh);
+                        sm.planes[25 * nbp + b] = (uint32_t)(kMagicBits - OFF * sm_);
+                        sm.planes[26 * nbp + b] = (uint32_t)(kMagicBits - OFF * sl);
+                    }
                     sm.planes[27 * nbp + b] = __float_as_uint(bad ? __int_as_float(0x7fc00000) : sb);
                 }
             }
@@ -532,24 +676,24 @@ __device__ __forceinline__ void plane_passes(const GemvArgs &a, const GemvSmem &
         }
 }
 
-template <int OFF>
+template <int QT>
 __device__ float build_planes(const GemvArgs &a, const GemvSmem &sm, uint32_t tid, uint32_t NC, bool prof,
                               unsigned long long &t_x, unsigned long long &t_b) {
     const bool norm = a.norm != 0;
-    const uint32_t nb = a.K >> 5, nbp = sm.nbp;
-    const uint32_t q = tid & 3, lane = tid & 31, warp = tid >> 5;
+    const uint32_t nb = a.K >> 5;
+    const uint32_t lane = tid & 31, warp = tid >> 5;
     const uint32_t per = NC >> 2;  // blocks per pass
     float ss = 0.f;
     for (uint32_t b0 = 0; b0 < nb;) {
         const uint32_t left = (nb - b0 + per - 1) / per;  // passes still needed
         if (left >= 3) {
-            plane_passes<OFF, 4>(a, sm, tid, b0, per, norm, ss, prof, t_x);
+            plane_passes<QT, 4>(a, sm, tid, b0, per, norm, ss, prof, t_x);
             b0 += 4 * per;
         } else if (left == 2) {
-            plane_passes<OFF, 2>(a, sm, tid, b0, per, norm, ss, prof, t_x);
+            plane_passes<QT, 2>(a, sm, tid, b0, per, norm, ss, prof, t_x);
             b0 += 2 * per;
         } else {
-            plane_passes<OFF, 1>(a, sm, tid, b0, per, norm, ss, prof, t_x);
+            plane_passes<QT, 1>(a, sm, tid, b0, per, norm, ss, prof, t_x);
             b0 += per;
         }
     }
@@ -610,8 +754,6 @@ __device__ bool gemv_consume(const GemvArgs &a, const GemvSmem &sm, uint32_t tid
     // per-thread row offsets (one copy of the row loop per quant type)
     const uint32_t MODE = a.mode;
     const bool PAIRED = MODE == GM_SWIGLU;
-    constexpr int BB = QTraits<QT>::BB;
-    constexpr int OFF = QTraits<QT>::OFF;
     constexpr uint32_t RPT = (uint32_t)QTraits<QT>::RPT >> (HALF ? 1 : 0);
     constexpr int RND = kRB / (int)RPT;  // rounds per reduction batch
     const uint32_t NC = blockDim.x, lane = tid & 31, warp = tid >> 5, NCW = NC >> 5;
@@ -641,7 +783,7 @@ __device__ bool gemv_consume(const GemvArgs &a, const GemvSmem &sm, uint32_t tid
     if (MODE == GM_PUSH) ll_tag = __ldcg(a.ll_epoch) + a.ll_k + 1;
 
     unsigned long long t_x = 0ull, t_b = 0ull;
-    const float rscale = build_planes<OFF>(a, sm, tid, NC, prof, t_x, t_b);
+    const float rscale = build_planes<QT>(a, sm, tid, NC, prof, t_x, t_b);
     XBlock xa, xb;
     load_planes(sm, unit_c, rscale, xa, xb);
 
@@ -675,14 +817,15 @@ __device__ bool gemv_consume(const GemvArgs &a, const GemvSmem &sm, uint32_t tid
     // half and the up rows in the second, local rows (gate, up, gate, up, ...)
     uint32_t off[RPT], cur[RPT];
     bool upper[RPT];
+    const uint32_t sub = unit_c & 3;  // K-quants: quarter of the superblock
 #pragma unroll
     for (uint32_t e = 0; e < RPT; ++e) {
         const uint32_t ls = slot_c * RPT + e;
         if (!PAIRED) {
-            off[e] = ls * rbytes + unit_c * (2 * BB);
+            off[e] = ls * rbytes + unit_bytes<QT>(unit_c);
             upper[e] = false;
         } else {
-            off[e] = (ls >> 1) * rbytes + unit_c * (2 * BB) + ((ls & 1) ? sbytes / 2 : 0u);
+            off[e] = (ls >> 1) * rbytes + unit_bytes<QT>(unit_c) + ((ls & 1) ? sbytes / 2 : 0u);
             upper[e] = ls & 1;
         }
     }
@@ -715,7 +858,7 @@ __device__ bool gemv_consume(const GemvArgs &a, const GemvSmem &sm, uint32_t tid
                 const uint8_t *sb = ring + rs.slot * sbytes;
 #pragma unroll
                 for (uint32_t e = 0; e < RPT; ++e) {
-                    const float d = unit_dot<QT, A4>(sb + cur[e], xa, xb, two);
+                    const float d = unit_dot<QT, A4>(sb + cur[e], xa, xb, two, sub);
                     acc[RPT * jj + e] = active ? d : 0.f;
                 }
                 __syncwarp();

@@ -105,7 +105,10 @@ bool ggml_block(uint32_t type, uint32_t &values, uint32_t &bytes) {
     case 0: values = 1; bytes = 4; return true;
     case 2: values = 32; bytes = 18; return true;
     case 6: values = 32; bytes = 22; return true;
+    case 7: values = 32; bytes = 24; return true;
     case 8: values = 32; bytes = 34; return true;
+    case 12: values = 256; bytes = 144; return true;
+    case 14: values = 256; bytes = 210; return true;
     default: return false;
     }
 }

@@ -18,10 +18,8 @@ __global__ void pf_embed_kernel(const uint8_t *table, uint32_t type, uint32_t co
                                 const uint32_t *tokens, float *x) {
     const uint32_t t = blockIdx.x;
     const uint8_t *row = table + (uint64_t)tokens[t] * row_bytes;
-    const uint32_t bb = type == 2 ? 18 : type == 6 ? 22 : 34;
     for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x)
-        x[(size_t)t * cols + i] = type == 0 ? reinterpret_cast<const float *>(row)[i]
-                                            : decode_value(row + (i >> 5) * bb, type, i & 31);
+        x[(size_t)t * cols + i] = type == 0 ? reinterpret_cast<const float *>(row)[i] : decode_elem(row, type, i);
 }
 
 __device__ __forceinline__ float pf_block_sum(float v, float *red) {

@@ -57,9 +57,16 @@ static const void *gemv_fn(int qt, int mode, bool a4, bool big) {
     case QT_Q4_0: return pick_gemv_mode<QT_Q4_0>(mode, a4, big);
     case QT_Q5_0: return pick_gemv_mode<QT_Q5_0>(mode, a4, big);
     case QT_Q8_0: return pick_gemv_mode<QT_Q8_0>(mode, a4, big);
+    // (their units are always 4-byte aligned, or loaded without that assumption)
+    case QT_Q5_1: return (const void *)gemv_kernel<QT_Q5_1, true>;
+    case QT_Q4_K: return (const void *)gemv_kernel<QT_Q4_K, true>;
+    case QT_Q6_K: return (const void *)gemv_kernel<QT_Q6_K, true>;
     default: return nullptr;
     }
 }
+
+// Values per block of a GEMV-able type (the input width must be a multiple).
+static uint32_t gemv_block_values(int qt) { return qt == QT_Q4_K || qt == QT_Q6_K ? 256u : 32u; }
 
 template <int HD>
 static const void *pick_attn_gq(uint32_t gq) {
@@ -126,7 +133,7 @@ constexpr uint32_t kMaxSmem = 227 * 1024;  // per-block opt-in limit (static + d
 static bool plan_gemv(int qt, int mode, int sms, GemvLaunch &L, bool half_rows = false) {
     GemvArgs &a = L.a;
     const uint32_t nb = a.K / 32;
-    if (a.K % 32 || nb == 0 || a.n_out == 0) { set_err("gemv: bad shape"); return false; }
+    if (a.K % gemv_block_values(qt) || nb == 0 || a.n_out == 0) { set_err("gemv: bad shape"); return false; }
     const bool paired = mode == GM_SWIGLU;
     a.mode = (uint32_t)mode;
     a.norm = (mode == GM_QKV || mode == GM_SWIGLU || mode == GM_LOGITS) ? 1u : 0u;
@@ -185,7 +192,7 @@ static bool g_attr_done[64];
 static bool set_smem_attrs(int dev) {
     if (dev < 0 || dev >= 64) return true;
     if (g_attr_done[dev]) return true;
-    const int qts[3] = {QT_Q4_0, QT_Q5_0, QT_Q8_0};
+    const int qts[6] = {QT_Q4_0, QT_Q5_0, QT_Q8_0, QT_Q5_1, QT_Q4_K, QT_Q6_K};
     for (int qt : qts)
         for (int mode = 0; mode <= GM_LOGITS; ++mode)
             for (int a4 = 0; a4 < 2; ++a4)
@@ -207,7 +214,10 @@ static bool block_bytes_of(uint32_t type, uint32_t &bb) {
     switch (type) {
     case 2: bb = 18; return true;
     case 6: bb = 22; return true;
+    case 7: bb = 24; return true;
     case 8: bb = 34; return true;
+    case 12: bb = 144; return true;
+    case 14: bb = 210; return true;
     default: return false;
     }
 }
@@ -231,8 +241,9 @@ static bool matvec_args_ok(const void *w, size_t w_size, uint32_t type, const vo
     // quant_matvec.c:270-289
     if (!w || !x || !y || in == 0 || out == 0) { set_err("quant_matvec: null pointer or zero size"); return false; }
     if (!block_bytes_of(type, bb)) { set_err("quant_matvec: unsupported ggml type"); return false; }
-    if (in % 32) { set_err("quant_matvec: input_size not a multiple of 32"); return false; }
-    const uint64_t rb = (uint64_t)(in / 32) * bb;
+    const uint32_t bv = gemv_block_values((int)type);
+    if (in % bv) { set_err("quant_matvec: input_size not a multiple of the block size"); return false; }
+    const uint64_t rb = (uint64_t)(in / bv) * bb;
     if (rb > UINT32_MAX || out > UINT32_MAX || out > SIZE_MAX / rb || w_size < out * rb) {
         set_err("quant_matvec: weights smaller than output_size rows");
         return false;
@@ -254,6 +265,10 @@ static bool matvec_dev(const void *w, size_t w_size, uint32_t type, const float 
     uint32_t bb, row_bytes;
     if (!matvec_args_ok(w, w_size, type, x, y, in, out, bb, row_bytes)) return false;
     if ((uintptr_t)w % 2) { set_err("quant_matvec_dev: weights must be 2-byte aligned"); return false; }
+    if ((type == 7 && (uintptr_t)w % 4) || (type == 12 && (uintptr_t)w % 16)) {
+        set_err("quant_matvec_dev: Q5_1 weights must be 4-byte and Q4_K weights 16-byte aligned");
+        return false;
+    }
     if ((uintptr_t)x % 16) { set_err("quant_matvec_dev: input must be 16-byte aligned"); return false; }
     if (span16(w, (uint64_t)out * row_bytes) > w_size) {
         set_err("quant_matvec_dev: weights_size must reach the 16-byte boundary after the last row (" +
@@ -392,6 +407,7 @@ struct Mat {
 
 struct LayerW {
     Mat qkv, o, gate, up, down;
+    Mat v;                // attn_v when its quant type differs from attn_q / attn_k (qkv then holds q|k)
     const float *attn_norm = nullptr, *ffn_norm = nullptr;
 };
 
@@ -547,8 +563,8 @@ static bool load_model(fwb_model *m, const char *path, size_t max_ctx) {
             !check_mat(t.v, KV * hd, E, "attn_v") || !check_mat(t.o, E, H * hd, "attn_output") ||
             !check_mat(t.g, F, E, "ffn_gate") || !check_mat(t.u, F, E, "ffn_up") || !check_mat(t.d, E, F, "ffn_down"))
             return false;
-        if (t.q->type != t.k->type || t.q->type != t.v->type || t.g->type != t.u->type) {
-            set_err("q/k/v (and gate/up) must share a quant type");
+        if (t.q->type != t.k->type || t.g->type != t.u->type) {
+            set_err("q/k (and gate/up) must share a quant type");
             return false;
         }
     }
@@ -568,8 +584,15 @@ static bool load_model(fwb_model *m, const char *path, size_t max_ctx) {
         const uint32_t cols = (uint32_t)t->dims[0], rows = t->n_dims >= 2 ? (uint32_t)t->dims[1] : 1u;
         return tp_shard_spec(c, t->name, rows, cols, rk, W, as_head);
     };
+    std::string shard_err;
+    auto whole_blocks = [&](const GgufTensor *t, const ShardSpec &sp) {
+        uint32_t v = 1, b = 4;
+        ggml_block(t->type, v, b);
+        if (sp.c0 % v || sp.c1 % v) shard_err = t->name + ": the rank's columns are not whole quant blocks";
+    };
     auto add = [&](const GgufTensor *t, bool as_head) {
         Pl e{t, 0, spec(t, as_head), 0};
+        whole_blocks(t, e.sp);
         e.bytes = tp_shard_bytes(*t, e.sp);
         e.off = place(e.bytes);
         plan.push_back(e);
@@ -592,13 +615,17 @@ static bool load_model(fwb_model *m, const char *path, size_t max_ctx) {
         pq.bytes = tp_shard_bytes(*t.q, pq.sp);
         pk.bytes = tp_shard_bytes(*t.k, pk.sp);
         pv.bytes = tp_shard_bytes(*t.v, pv.sp);
-        const uint64_t oq = place(pq.bytes + pk.bytes + pv.bytes);
+        // q, k (and v of the same type) adjacent: one [q|k|v] matrix; a v of
+        // another type (the Q4_K_M mixes) is a matrix of its own
+        const bool v_split = t.v->type != t.q->type;
+        const uint64_t oq = place(pq.bytes + pk.bytes + (v_split ? 0 : pv.bytes));
         pq.off = oq;
         pk.off = oq + pq.bytes;
-        pv.off = oq + pq.bytes + pk.bytes;
+        pv.off = v_split ? place(pv.bytes) : oq + pq.bytes + pk.bytes;
         plan.push_back(pq); plan.push_back(pk); plan.push_back(pv);
         uint64_t *L = &lo[l * 8];
         L[0] = oq;
+        L[7] = v_split ? pv.off : 0;
         L[1] = add(t.o, false).off;
         L[2] = add(t.g, false).off;
         L[3] = add(t.u, false).off;
@@ -609,6 +636,7 @@ static bool load_model(fwb_model *m, const char *path, size_t max_ctx) {
             if (plan[i].t != t.an && plan[i].t != t.fn) m->weight_bytes += plan[i].bytes;
         m->weight_bytes += t.an->bytes + t.fn->bytes;
     }
+    if (!shard_err.empty()) { set_err("tensor parallel: " + shard_err); return false; }
     const uint64_t arena_bytes = off + 256;
     if (!dalloc(m, (void **)&m->arena, arena_bytes)) return false;
 
@@ -656,7 +684,9 @@ static bool load_model(fwb_model *m, const char *path, size_t max_ctx) {
         LT &t = lt[l];
         uint64_t *L = &lo[l * 8];
         LayerW &w = m->layers[l];
-        w.qkv = mat(t.q, L[0], (Hr + 2 * KVr) * hd, E);
+        const bool v_split = t.v->type != t.q->type;
+        w.qkv = mat(t.q, L[0], (Hr + (v_split ? 1 : 2) * KVr) * hd, E);
+        if (v_split) w.v = mat(t.v, L[7], KVr * hd, E);
         w.o = mat(t.o, L[1], E, Hr * hd);
         w.gate = mat(t.g, L[2], Fr, E);
         w.up = mat(t.u, L[3], Fr, E);
@@ -847,6 +877,13 @@ static bool build_steps(fwb_model *m) {
         const std::string p = "L" + std::to_string(l) + ".";
         if (!gemv_step(p + "qkv_rope", GM_QKV, w.qkv, nullptr, w.qkv.rows, m->x, w.attn_norm, nullptr, ex))
             return false;
+        if (w.v.p) {  // v rows of their own type: every row of this GEMV is a v row
+            GemvArgs ev = ex;
+            ev.n_q = 0;
+            ev.n_kv = 0;
+            if (!gemv_step(p + "v", GM_QKV, w.v, nullptr, w.v.rows, m->x, w.attn_norm, nullptr, ev)) return false;
+            m->steps.back().phase.nobar = 1;  // independent of the q|k phase: no barrier between them
+        }
         {
             Step s;
             s.name = p + "attention";
@@ -1295,8 +1332,9 @@ int quant_gemm_dev(const void *d_weights, size_t weights_size, uint32_t ggml_typ
 int quant_dequant_dev(const void *d_weights, size_t weights_size, uint32_t ggml_type, float *d_out, size_t n_values,
                       void *stream) {
     uint32_t bb;
-    if (!d_weights || !d_out || !n_values || n_values % 32 || !block_bytes_of(ggml_type, bb) ||
-        weights_size < n_values / 32 * bb) {
+    if (!d_weights || !d_out || !n_values || !block_bytes_of(ggml_type, bb) ||
+        n_values % gemv_block_values((int)ggml_type) ||
+        weights_size < n_values / gemv_block_values((int)ggml_type) * bb) {
         set_err("quant_dequant_dev: bad arguments");
         return -1;
     }
@@ -1441,6 +1479,8 @@ int fwb_model_kernels_per_step(const fwb_model_t *m) {
 static bool prefill_eligible(const fwb_model *m) {
     const ModelConfig &c = m->cfg;
     if (m->world != 1 || c.head_dim > 128 || c.head_dim % 4 || c.n_head % c.n_head_kv) return false;
+    for (const LayerW &w : m->layers)
+        if (w.v.p) return false;  // a v matrix of another type than q / k
     for (const LayerW &w : m->layers)
         for (const Mat *t : {&w.qkv, &w.o, &w.gate, &w.up, &w.down})
             if (t->type != 2 || t->cols % kTcK || (uintptr_t)t->p % 4) return false;

@@ -13,8 +13,9 @@
 // in 256 bins; the draw is located the same way inside the nucleus.  Sums
 // are kept in 40-bit fixed point (u64), so they do not depend on the order
 // of the atomic adds: the result is deterministic.  It can differ from the
-// reference's fp32 running sums only where the draw or top_p falls within
-// about 1e-7 of a cumulative boundary.
+// reference only where the draw or top_p falls within the rounding drift of
+// the reference's fp32 running sum (~1e-6 of the total over a nucleus of
+// thousands of tokens) of a cumulative boundary.
 #pragma once
 #include <cuda_fp16.h>
 #include <cstdint>

@@ -8,9 +8,15 @@ from __future__ import annotations
 
 from dataclasses import dataclass, field, replace
 
-F32, Q4_0, Q5_0, Q8_0 = 0, 2, 6, 8
-TYPE_NAMES = {F32: "F32", Q4_0: "Q4_0", Q5_0: "Q5_0", Q8_0: "Q8_0"}
-BLOCK_BYTES = {Q4_0: 18, Q5_0: 22, Q8_0: 34}
+F32, Q4_0, Q5_0, Q5_1, Q8_0, Q4_K, Q6_K = 0, 2, 6, 7, 8, 12, 14
+TYPE_NAMES = {F32: "F32", Q4_0: "Q4_0", Q5_0: "Q5_0", Q5_1: "Q5_1", Q8_0: "Q8_0", Q4_K: "Q4_K", Q6_K: "Q6_K"}
+BLOCK_BYTES = {Q4_0: 18, Q5_0: 22, Q5_1: 24, Q8_0: 34, Q4_K: 144, Q6_K: 210}
+BLOCK_VALUES = {Q4_0: 32, Q5_0: 32, Q5_1: 32, Q8_0: 32, Q4_K: 256, Q6_K: 256}
+
+
+def quant_bytes(t: int, n: int) -> int:
+    """Bytes of n values of ggml type t (n a multiple of the block)."""
+    return n * 4 if t == F32 else n // BLOCK_VALUES[t] * BLOCK_BYTES[t]
 
 
 @dataclass(frozen=True)
@@ -46,9 +52,7 @@ class ModelShape:
         return self.n_embd // self.n_head
 
     def tensor_bytes(self, t: int, rows: int, cols: int) -> int:
-        if t == F32:
-            return rows * cols * 4
-        return rows * cols // 32 * BLOCK_BYTES[t]
+        return quant_bytes(t, rows * cols)
 
     def weight_bytes_per_token(self) -> int:
         """Algorithmic HBM bytes one decode step must stream: every quantised
@@ -103,13 +107,21 @@ SMALL_MIXED = replace(SMALL_Q4_0, name="small-mixed", t_q=Q8_0, t_k=Q8_0, t_v=Q8
                       t_gate=Q5_0, t_up=Q5_0, t_down=Q8_0, t_out=Q8_0)
 SMALL_TIED_Q8 = replace(TINY, name="small-tied-q8_0", n_layer=2, n_vocab=1000, n_ctx=128)
 SMALL_NO_OUT_NORM = replace(SMALL_Q4_0, name="small-q4_0-no-out-norm", out_norm=False)
+# the K-quant mix of a Q4_K_M file: Q4_K attention/gate/up, Q6_K down / v /
+# head, Q4_K embedding; widths multiples of 256
+SMALL_KQUANT = ModelShape("small-kquant", n_embd=512, n_layer=2, n_head=4, n_head_kv=2, n_ff=1536,
+                          n_vocab=2048, n_ctx=512, rope_base=500000.0, t_embd=Q4_K, t_q=Q4_K, t_k=Q4_K,
+                          t_v=Q6_K, t_o=Q4_K, t_gate=Q4_K, t_up=Q4_K, t_down=Q6_K, t_out=Q6_K)
+SMALL_Q5_1 = replace(SMALL_Q4_0, name="small-q5_1", t_q=Q5_1, t_k=Q5_1, t_v=Q5_1, t_o=Q5_1, t_gate=Q5_1,
+                     t_up=Q5_1, t_down=Q5_1, t_out=Q5_1, t_embd=Q5_1)
 # splits over 2, 4 or 8 tensor-parallel ranks (8 KV heads, 256 FFN rows and
 # 256 vocabulary rows per rank at 8 ranks)
 SMALL_TP8 = ModelShape("small-tp8", n_embd=1024, n_layer=2, n_head=8, n_head_kv=8, n_ff=2048,
                        n_vocab=2048, n_ctx=512, rope_base=500000.0)
 
 CONFIGS = {c.name: c for c in (TINY, LLAMA8B_Q4_0, LLAMA8B_MIXED, LLAMA70B_Q4_0, SMALL_TP8,
-                               SMALL_Q4_0, SMALL_MIXED, SMALL_TIED_Q8, SMALL_NO_OUT_NORM)}
+                               SMALL_Q4_0, SMALL_MIXED, SMALL_TIED_Q8, SMALL_NO_OUT_NORM, SMALL_KQUANT,
+                               SMALL_Q5_1)}
 
 
 def with_layers(cfg: ModelShape, n_layer: int) -> ModelShape:

@@ -20,7 +20,7 @@ import struct
 import numpy as np
 
 from . import native
-from .configs import BLOCK_BYTES, F32, ModelShape
+from .configs import F32, ModelShape, quant_bytes
 
 ALIGN = 32
 _GGUF_MAGIC = 0x46554747
@@ -87,7 +87,7 @@ def tensor_plan(cfg: ModelShape) -> list[tuple[str, int, int, int, str]]:
 
 
 def _nbytes(t: int, rows: int, cols: int) -> int:
-    return rows * cols * 4 if t == F32 else rows * cols // 32 * BLOCK_BYTES[t]
+    return quant_bytes(t, rows * cols)
 
 
 def write_model(path: str, cfg: ModelShape, seed: int = 1234) -> str:

@@ -218,10 +218,12 @@ int fwb_generate_greedy(fwb_model_t *m, uint32_t first_token, size_t pos0, size_
  * (sampler_top_p, sampler.c:46-84) with one draw of the reference's
  * xorshift64 generator, whose state *rng_state advances exactly as the
  * reference's does (only when temperature > 0).  The nucleus and the draw
- * are found by radix selection with fixed-point sums instead of a sort of
- * the vocabulary; the token can differ from the reference's only where the
- * draw or top_p falls within about 1e-7 of a cumulative probability
- * boundary.  Under tensor parallelism every rank makes the same call (the
+ * are found by radix selection with exact fixed-point sums instead of a
+ * sort of the vocabulary and the reference's fp32 running sum; the token can
+ * differ from the reference's only where the draw or top_p falls within that
+ * sum's rounding drift of a cumulative probability boundary (about 1e-6 of
+ * the total for a nucleus of thousands of tokens, far less for peaked
+ * distributions).  Under tensor parallelism every rank makes the same call (the
  * other ranks' logits are read over NVLink).  Synchronous.
  */
 int fwb_sample(fwb_model_t *m, const uint32_t *history, size_t n_history, float temperature, float top_p,

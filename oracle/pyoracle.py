@@ -202,6 +202,26 @@ def quant_matvec(w: np.ndarray, t: int, x: np.ndarray, n_out: int, use_ref: bool
     return y
 
 
+_REF_DECODERS = {7: "q5_1_decode", 8: "q8_0_decode", 12: "q4_k_decode", 14: "q6_k_decode"}
+_REF_BLOCK = {7: (32, 24), 8: (32, 34), 12: (256, 144), 14: (256, 210)}
+
+
+def ref_dequant(w: np.ndarray, t: int, n: int) -> np.ndarray:
+    """n values of type t decoded by the compiled reference's own decoders
+    (quant.c: q5_1_decode, q8_0_decode, q4_k_decode, q6_k_decode)."""
+    lib = ref_lib()
+    fn = getattr(lib, _REF_DECODERS[t])
+    fn.argtypes = [_c.c_void_p, _c.c_size_t, _fp, _c.c_size_t]
+    fn.restype = _c.c_int
+    bv, bb = _REF_BLOCK[t]
+    nbytes = n // bv * bb
+    src = np.ascontiguousarray(w[:nbytes])
+    out = np.zeros(n, np.float32)
+    if fn(src.ctypes.data, nbytes, _f(out), n) != 0:
+        raise RuntimeError("reference decoder rejected its arguments")
+    return out
+
+
 def dequant(w: np.ndarray, t: int, n: int) -> np.ndarray:
     out = np.zeros(n, np.float32)
     if oracle_lib().orc_dequant(w.ctypes.data, w.nbytes, t, _f(out), n) != 0:
