@@ -43,11 +43,12 @@ int fwb_device_count(void);
  * of GGUF blocks (row r at r * (input_size/32) * block_bytes), input[in] and
  * output[out] are host fp32 arrays.  The call copies weights and input to the
  * current device, runs the GEMV there and copies output back.
- * Types: 2 (Q4_0), 6 (Q5_0), 8 (Q8_0).  The reference instead supports
- * 6, 7 (Q5_1), 8, 12 (Q4_K), 14 (Q6_K) and lacks Q4_0.
+ * Types: 2 (Q4_0), 6 (Q5_0), 7 (Q5_1), 8 (Q8_0), 12 (Q4_K), 14 (Q6_K): the
+ * reference's set (quant_matvec.c:52-62) plus GGML's Q4_0, which the
+ * reference lacks.
  * Returns -1 for NULL pointers, zero sizes, an unsupported type,
- * input_size % 32 != 0 or weights_size < output_size * row bytes, like the
- * reference.
+ * input_size not a multiple of the block (32 values; 256 for Q4_K / Q6_K)
+ * or weights_size < output_size * row bytes, like the reference.
  */
 int quant_matvec(const void *weights, size_t weights_size, uint32_t ggml_type,
                  const float *input, float *output, size_t input_size,
@@ -91,7 +92,8 @@ int quant_matvec_static(const void *weights, size_t weights_size, uint32_t ggml_
 /*
  * Device-pointer form of quant_matvec for callers whose data already lives
  * in HBM; no reference counterpart (quant_matvec.h:7-15 is host-only).
- * d_weights must be 2-byte aligned.  The kernel copies 16-byte aligned
+ * d_weights must be 2-byte aligned (4-byte for Q5_1, 16-byte for Q4_K).
+ * The kernel copies 16-byte aligned
  * supersets of the rows: it reads from d_weights rounded down to 16 bytes
  * (inside the same allocation unless d_weights is 16-byte aligned, as
  * cudaMalloc pointers are) up to the 16-byte boundary at or after the last
@@ -130,9 +132,10 @@ int quant_gemm_dev(const void *d_weights, size_t weights_size, uint32_t ggml_typ
                    void *stream);
 
 /*
- * Dequantise n_values (a multiple of 32) from Q4_0 / Q5_0 / Q8_0 blocks into
- * fp32 on the device, bit-identical to the reference decoders (q8_0_decode
- * quant.c:232-263, q5_0_decode linear.c:40-56, and GGML's Q4_0).
+ * Dequantise n_values (a multiple of the block) from Q4_0 / Q5_0 / Q5_1 /
+ * Q8_0 / Q4_K / Q6_K blocks into fp32 on the device, bit-identical to the
+ * reference decoders (quant.c: q5_1_decode, q8_0_decode, q4_k_decode,
+ * q6_k_decode; q5_0 as linear.c:40-56; GGML's Q4_0).
  */
 int quant_dequant_dev(const void *d_weights, size_t weights_size, uint32_t ggml_type,
                       float *d_out, size_t n_values, void *stream);
