@@ -9,19 +9,25 @@
 // contraction is dense enough for the tensor cores, unlike batch-1 decode.
 //
 // Tile: 128 tokens (TMEM lanes) x 128 weight rows (TMEM columns) per CTA, K
-// in steps of 64 (two Q4_0 blocks).  Four warps load the step's activation
-// rows and dequantise the weight rows ((q - 8) * d in fp32, as the reference
-// decoders, then rounded to fp16) into shared memory in the K-major 128-byte
-// swizzled layout the MMA reads; one thread issues four
-// tcgen05.mma.kind::f16 (K = 16 each) and commits them to an mbarrier.  Two
-// stages: the loads of step i+1 overlap the MMAs of step i, and each thread
-// has step i+1's global bytes in flight while it writes step i's tiles.  The epilogue
-// reads the accumulator with tcgen05.ld (warp w owns TMEM lanes 32w..32w+31)
-// and stores, or adds into, Y.
+// in steps of 64 (two Q4_0 blocks) through a ring of kTcStages shared-memory
+// stages, two CTAs per SM.  Warp-specialised: four producer warps fill a
+// stage -- thread t copies token row t's 64 activations and dequantises
+// weight row t's two blocks, (q - 8) * d rounded once to fp16 with half2
+// arithmetic (bit-identical to rounding the exact fp32 product), into the
+// K-major 128-byte-swizzled layout the MMA reads -- and signal the stage's
+// `full` mbarrier; one thread of the fifth warp issues four
+// tcgen05.mma.kind::f16 (K = 16 each) per stage and commits them to the
+// stage's `empty` mbarrier, which the producers wait on before refilling it.
+// Producers fetch the next stage's activation row and the next 256-wide K
+// chunk of their weight row (144 bytes, 16-byte loads when the rows allow)
+// one step ahead.  After the last MMA a commit to `done` releases the
+// epilogue: the producer warps read the accumulator with tcgen05.ld (warp w
+// owns TMEM lanes 32w..32w+31) and store, or add into, Y.
 //
 // Numerics: fp16 weights carry (q - 8) * d to 11 significant bits and fp16
 // activations x to 11 bits; products and sums are fp32.  Every wait is
-// bounded and sets an error bit; the TMEM columns are released on every path.
+// bounded and sets an error bit; the MMA thread always makes the final
+// commit, so the TMEM columns are released only after every issued MMA.
 #pragma once
 #include "common.cuh"
 
@@ -30,9 +36,11 @@ namespace fwb {
 constexpr uint32_t kTcM = 128;        // tokens per tile
 constexpr uint32_t kTcN = 128;        // weight rows per tile
 constexpr uint32_t kTcK = 64;         // K per stage
-constexpr uint32_t kTcThreads = 128;
+constexpr uint32_t kTcStages = 3;     // ring depth (two CTAs per SM)
+constexpr uint32_t kTcProducers = 128;  // four producer warps; a fifth issues the MMAs
+constexpr uint32_t kTcThreads = kTcProducers + 32;
 constexpr uint32_t kTcTileBytes = 128 * 128;  // 128 rows of 64 fp16 (128 B)
-constexpr uint32_t kTcSmem = 4 * kTcTileBytes + 1024 + 256;  // 2 stages x (A, B), alignment, barriers
+constexpr uint32_t kTcSmem = kTcStages * 2 * kTcTileBytes + 1024 + 256;  // stages x (A, B), alignment, barriers
 
 enum TcMode : uint32_t { TC_STORE = 0, TC_ADD = 1 };
 
@@ -98,91 +106,99 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
     return *reinterpret_cast<const uint32_t *>(&h);
 }
 
-// The global bytes of one stage for this thread: its activation row (64 fp16)
-// and its weight row's two Q4_0 blocks (36 bytes, 4-byte aligned).  Fetched
-// one stage ahead so that their latency hides behind the current stage.
-struct TcRaw {
-    uint4 a[8];
-    uint32_t q[9];
-};
-
-__device__ __forceinline__ void tc_fetch(const TcArgs &a, uint32_t m0, uint32_t n0, uint32_t k0, TcRaw &r) {
-    const uint32_t t = threadIdx.x, m = m0 + t, n = n0 + t;
-    if (m < a.M) {
-        const uint4 *src = reinterpret_cast<const uint4 *>(a.x + (size_t)m * a.K + k0);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) r.a[i] = __ldg(src + i);
-    } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) r.a[i] = make_uint4(0u, 0u, 0u, 0u);
-    }
-    if (n < a.N) {
-        const uint32_t *src = reinterpret_cast<const uint32_t *>(a.w + (size_t)n * a.row_bytes + (k0 >> 5) * 18u);
-#pragma unroll
-        for (int i = 0; i < 9; ++i) r.q[i] = __ldg(src + i);
-    } else {
-#pragma unroll
-        for (int i = 0; i < 9; ++i) r.q[i] = 0u;  // d = 0: every value 0
-    }
+// Two fp16 values (q - 8) * d from the nibbles of bytes b and b + 1 of word
+// x (byte b = 0 or 2): (1024 + q) as fp16 bits, minus 1032, times d -- each
+// step exact but the last, which rounds the exact product once.
+template <bool HIGH>
+__device__ __forceinline__ uint32_t q4_pair(uint32_t x, uint32_t sel, __half2 d2) {
+    uint32_t p = __byte_perm(x, 0u, sel);  // byte b -> byte 0, byte b+1 -> byte 2
+    if (HIGH) p >>= 4;
+    p = (p & 0x000F000Fu) | 0x64006400u;
+    const __half2 v = __hmul2(__hsub2(*reinterpret_cast<const __half2 *>(&p), __float2half2_rn(1032.0f)), d2);
+    return *reinterpret_cast<const uint32_t *>(&v);
 }
 
-// One stage into the swizzled A / B tiles: the activation row as is, the
-// weight row dequantised (rows outside M / N are zero).
-__device__ __forceinline__ void tc_store_stage(const TcRaw &r, uint8_t *sa, uint8_t *sb) {
-    const uint32_t t = threadIdx.x;
-#pragma unroll
-    for (uint32_t i = 0; i < 8; ++i) *reinterpret_cast<uint4 *>(sa + tc_sw128(t, i)) = r.a[i];
-    // block 0: d in q[0] low half, quants in bytes 2..17; block 1: d in q[4]
-    // high half, quants in bytes 20..35 = q[5..8]
-    const float d0 = __half2float(__ushort_as_half((unsigned short)(r.q[0] & 0xffffu)));
-    const float d1 = __half2float(__ushort_as_half((unsigned short)(r.q[4] >> 16)));
-    uint32_t qs0[4], qs1[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        qs0[i] = __funnelshift_r(r.q[i], r.q[i + 1], 16);
-        qs1[i] = r.q[5 + i];
-    }
+// Weight row t of one K step (two Q4_0 blocks in 9 words, the first block's
+// scale in the low half of w[0], the second's in the high half of w[4]) into
+// the swizzled B tile: 8 chunks of 8 fp16.
+__device__ __forceinline__ void tc_dequant_row(const uint32_t (&w)[9], uint8_t *sb, uint32_t t) {
 #pragma unroll
     for (uint32_t blk = 0; blk < 2; ++blk) {
-        const uint32_t *qs = blk ? qs1 : qs0;
-        const float d = blk ? d1 : d0;
-        // element j (< 16): low nibble of byte j; element j + 16: high nibble
+        const uint32_t dbits = blk ? (w[4] >> 16) : (w[0] & 0xffffu);
+        const __half dh = __ushort_as_half((unsigned short)dbits);
+        const __half2 d2 = __halves2half2(dh, dh);
+        uint32_t qs[4];
 #pragma unroll
-        for (uint32_t half = 0; half < 2; ++half) {
+        for (int i = 0; i < 4; ++i) qs[i] = blk ? w[5 + i] : __funnelshift_r(w[i], w[i + 1], 16);
+        // element j < 16: low nibble of byte j; element 16 + j: high nibble
 #pragma unroll
-            for (uint32_t cc = 0; cc < 2; ++cc) {  // 8 elements per chunk
-                uint32_t o[4];
-#pragma unroll
-                for (uint32_t e = 0; e < 4; ++e) {
-                    float v[2];
-#pragma unroll
-                    for (uint32_t u = 0; u < 2; ++u) {
-                        const uint32_t j = cc * 8 + e * 2 + u;  // byte index 0..15
-                        const uint32_t byte = (qs[j >> 2] >> ((j & 3) * 8)) & 0xffu;
-                        const int qv = (int)(half ? (byte >> 4) : (byte & 15u)) - 8;
-                        v[u] = __fmul_rn((float)qv, d);
-                    }
-                    o[e] = pack_h2(v[0], v[1]);
-                }
-                const uint32_t chunk = blk * 4 + half * 2 + cc;
-                *reinterpret_cast<uint4 *>(sb + tc_sw128(t, chunk)) = make_uint4(o[0], o[1], o[2], o[3]);
+        for (uint32_t c = 0; c < 4; ++c) {
+            const uint32_t x0 = qs[(c & 1) * 2], x1 = qs[(c & 1) * 2 + 1];
+            uint4 o;
+            if (c < 2) {
+                o.x = q4_pair<false>(x0, 0x4140u, d2); o.y = q4_pair<false>(x0, 0x4342u, d2);
+                o.z = q4_pair<false>(x1, 0x4140u, d2); o.w = q4_pair<false>(x1, 0x4342u, d2);
+            } else {
+                o.x = q4_pair<true>(x0, 0x4140u, d2); o.y = q4_pair<true>(x0, 0x4342u, d2);
+                o.z = q4_pair<true>(x1, 0x4140u, d2); o.w = q4_pair<true>(x1, 0x4342u, d2);
             }
+            *reinterpret_cast<uint4 *>(sb + tc_sw128(t, blk * 4 + c)) = o;
         }
     }
 }
 
-__global__ void __launch_bounds__(kTcThreads, 1) gemm_q4_0_tc_kernel(const __grid_constant__ TcArgs a) {
+// This producer thread's activation row of K step k0 (64 fp16; zeros
+// outside M).
+__device__ __forceinline__ void tc_fetch_a(const TcArgs &a, uint32_t m, uint32_t k0, uint4 (&r)[8]) {
+    if (m < a.M) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(a.x + (size_t)m * a.K + k0);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) r[i] = __ldg(src + i);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) r[i] = make_uint4(0u, 0u, 0u, 0u);
+    }
+}
+
+// 4 K steps (one 256-wide chunk, 36 words) of this producer's weight row
+// (zeros -- scale 0 -- outside N or beyond the last K step).  V16: the row's
+// chunks are 16-byte aligned (row bytes and base multiples of 16).
+template <bool V16>
+__device__ __forceinline__ void tc_fetch_w(const TcArgs &a, uint32_t n, uint32_t step0, uint32_t steps,
+                                           uint32_t (&w)[36]) {
+    const uint8_t *row = a.w + (size_t)n * a.row_bytes + (size_t)step0 * 36u;
+    if (n < a.N && V16 && step0 + 4 <= steps) {
+#pragma unroll
+        for (int i = 0; i < 9; ++i) {
+            const uint4 v = __ldg(reinterpret_cast<const uint4 *>(row) + i);
+            w[4 * i] = v.x; w[4 * i + 1] = v.y; w[4 * i + 2] = v.z; w[4 * i + 3] = v.w;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 36; ++i)
+            w[i] = (n < a.N && step0 + (uint32_t)i / 9u < steps) ? __ldg(reinterpret_cast<const uint32_t *>(row) + i)
+                                                                 : 0u;
+    }
+}
+
+template <bool V16>
+__global__ void __launch_bounds__(kTcThreads, 2) gemm_q4_0_tc_kernel(const __grid_constant__ TcArgs a) {
     extern __shared__ uint8_t tc_smem_raw[];
     const uint32_t base = (smem_u32(tc_smem_raw) + 1023u) & ~1023u;
     uint8_t *smem = tc_smem_raw + (base - smem_u32(tc_smem_raw));
-    uint64_t *bar = reinterpret_cast<uint64_t *>(smem + 4 * kTcTileBytes);
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + 4 * kTcTileBytes + 64);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kTcStages * 2 * kTcTileBytes);
+    uint64_t *empty = full + kTcStages, *done = empty + kTcStages;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t n0 = blockIdx.x * kTcN, m0 = blockIdx.y * kTcM;
+    const uint32_t steps = a.K / kTcK;
 
     if (tid == 0) {
-        mbar_init(&bar[0], 1);
-        mbar_init(&bar[1], 1);
+        for (uint32_t s = 0; s < kTcStages; ++s) {
+            mbar_init(&full[s], kTcProducers / 32);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(done, 1);
         fence_mbar_init();
     }
     if (warp == 0) {  // 128 fp32 accumulator columns
@@ -195,56 +211,103 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q4_0_tc_kernel(const __gri
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-
-    const uint32_t steps = a.K / kTcK;
     bool ok = true;
-    TcRaw raw;
-    if (steps > 0) tc_fetch(a, m0, n0, 0, raw);
-    for (uint32_t it = 0; it < steps; ++it) {
-        const uint32_t s = it & 1u;
-        uint8_t *sa = smem + s * 2u * kTcTileBytes, *sb = sa + kTcTileBytes;  // stage s: A then B
-        TcRaw next = raw;
-        if (it + 1 < steps) tc_fetch(a, m0, n0, (it + 1) * kTcK, next);
-        if (it >= 2 && ok)  // the MMAs that read this stage two steps ago are done
-            ok = mbar_wait(&bar[s], ((it - 2) >> 1) & 1u, a.err, ERR_WAIT_FULL);
-        tc_store_stage(raw, sa, sb);
-        raw = next;
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core reads
-        __syncthreads();
-        if (tid == 0) {
-            tc_fence_after();
-            const uint64_t da = tc_desc(smem_u32(sa)), db = tc_desc(smem_u32(sb));
+
+    if (warp == kTcProducers / 32) {
+        // ---- MMA issue: one thread
+        if (lane == 0) {
+            uint32_t i = 0;
+            for (; i < steps; ++i) {
+                const uint32_t s = i % kTcStages;
+                if (!mbar_wait(&full[s], (i / kTcStages) & 1u, a.err, ERR_WAIT_FULL)) { ok = false; break; }
+                tc_fence_after();
+                uint8_t *sa = smem + s * 2u * kTcTileBytes, *sb = sa + kTcTileBytes;
+                const uint64_t da = tc_desc(smem_u32(sa)), db = tc_desc(smem_u32(sb));
 #pragma unroll
-            for (uint32_t k = 0; k < kTcK / 16; ++k)  // 16 fp16 = 32 bytes = 2 descriptor units per step
-                tc_mma(tmem, da + 2u * k, db + 2u * k, (it | k) != 0u);
-            tc_commit(&bar[s]);
+                for (uint32_t k = 0; k < kTcK / 16; ++k)  // 16 fp16 = 32 bytes = 2 descriptor units
+                    tc_mma(tmem, da + 2u * k, db + 2u * k, (i | k) != 0u);
+                tc_commit(&empty[s]);
+            }
+            tc_commit(done);  // covers every MMA issued above, also after a failed wait
         }
-    }
-    // the last commit covers every MMA issued before it
-    if (steps > 0 && ok) ok = mbar_wait(&bar[(steps - 1) & 1u], ((steps - 1) >> 1) & 1u, a.err, ERR_WAIT_FULL);
-    // a thread whose wait failed must not free TMEM the MMAs may still write
-    // to: it waits (bounded) again with the others below before the release
-    tc_fence_after();
-    if (ok && steps > 0) {
-        const uint32_t m = m0 + warp * 32 + lane;
-#pragma unroll 1
-        for (uint32_t c0 = 0; c0 < kTcN; c0 += 32) {
-            float v[32];
-            tc_ld32(tmem + ((warp * 32u) << 16) + c0, v);
-            if (m < a.M) {
-                float *yr = a.y + (size_t)m * a.ldy + n0 + c0;
+        __syncwarp();
+    } else {
+        // ---- producers: thread t fills token row t and weight row t of each stage
+        const uint32_t t = tid, m = m0 + t, n = n0 + t;
+        uint4 ar[8];
+        uint32_t wc[36];
+        if (steps) {
+            tc_fetch_a(a, m, 0, ar);
+            tc_fetch_w<V16>(a, n, 0, steps, wc);
+        }
+        for (uint32_t c0 = 0; c0 < steps && ok; c0 += 4) {
+            uint32_t wn[36];
+            tc_fetch_w<V16>(a, n, c0 + 4, steps, wn);  // zeros past the last step
 #pragma unroll
-                for (uint32_t i = 0; i < 32; ++i)
-                    if (n0 + c0 + i < a.N) yr[i] = a.mode == TC_ADD ? __fadd_rn(yr[i], v[i]) : v[i];
+            for (uint32_t j = 0; j < 4; ++j) {  // fully unrolled: wc is indexed by constants only
+                const uint32_t i = c0 + j;
+                if (i < steps && ok) {
+                    const uint32_t s = i % kTcStages;
+                    uint4 an[8];
+                    tc_fetch_a(a, m, i + 1 < steps ? (i + 1) * kTcK : i * kTcK, an);
+                    if (i >= kTcStages)  // the MMAs that read this stage kTcStages steps ago are done
+                        ok = __all_sync(0xffffffffu, mbar_wait(&empty[s], ((i / kTcStages) - 1) & 1u, a.err,
+                                                               ERR_WAIT_EMPTY));
+                    if (ok) {
+                        uint8_t *sa = smem + s * 2u * kTcTileBytes, *sb = sa + kTcTileBytes;
+#pragma unroll
+                        for (uint32_t q = 0; q < 8; ++q) *reinterpret_cast<uint4 *>(sa + tc_sw128(t, q)) = ar[q];
+                        const uint32_t w9[9] = {wc[9 * j], wc[9 * j + 1], wc[9 * j + 2], wc[9 * j + 3], wc[9 * j + 4],
+                                                wc[9 * j + 5], wc[9 * j + 6], wc[9 * j + 7], wc[9 * j + 8]};
+                        tc_dequant_row(w9, sb, t);
+                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic -> tensor core
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&full[s]);
+                    }
+#pragma unroll
+                    for (uint32_t q = 0; q < 8; ++q) ar[q] = an[q];
+                }
+            }
+#pragma unroll
+            for (uint32_t q = 0; q < 36; ++q) wc[q] = wn[q];
+        }
+        // ---- epilogue: the accumulator, once every MMA is done
+        const bool fin = __all_sync(0xffffffffu, mbar_wait(done, 0u, a.err, ERR_WAIT_FULL));
+        tc_fence_after();
+        if (ok && fin && steps > 0) {
+            const uint32_t mm = m0 + warp * 32 + lane;
+            const bool vec = (a.ldy & 3u) == 0u && ((uintptr_t)a.y & 15u) == 0u;
+#pragma unroll 1
+            for (uint32_t c0 = 0; c0 < kTcN; c0 += 32) {
+                float v[32];
+                tc_ld32(tmem + ((warp * 32u) << 16) + c0, v);  // warp w reads TMEM lanes 32w..32w+31
+                if (mm >= a.M) continue;
+                float *yr = a.y + (size_t)mm * a.ldy + n0 + c0;
+                if (vec && n0 + c0 + 32 <= a.N) {  // the thread's 128 contiguous bytes as 8 float4
+#pragma unroll
+                    for (uint32_t i = 0; i < 32; i += 4) {
+                        float4 o = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+                        if (a.mode == TC_ADD) {
+                            const float4 y0 = *reinterpret_cast<const float4 *>(yr + i);
+                            o.x = __fadd_rn(y0.x, o.x); o.y = __fadd_rn(y0.y, o.y);
+                            o.z = __fadd_rn(y0.z, o.z); o.w = __fadd_rn(y0.w, o.w);
+                        }
+                        *reinterpret_cast<float4 *>(yr + i) = o;
+                    }
+                } else {
+#pragma unroll
+                    for (uint32_t i = 0; i < 32; ++i)
+                        if (n0 + c0 + i < a.N) yr[i] = a.mode == TC_ADD ? __fadd_rn(yr[i], v[i]) : v[i];
+                }
             }
         }
     }
     tc_fence_before();
     __syncthreads();
-    if (!ok && tid == 0 && steps > 0)  // drain: the final commit must have landed before the release
-        mbar_wait(&bar[(steps - 1) & 1u], ((steps - 1) >> 1) & 1u, a.err, ERR_WAIT_DRAIN);
-    __syncthreads();
     if (warp == 0) {
+        // normally complete already; after a failed wait, the MMAs the final
+        // commit covers must finish before their columns are freed
+        mbar_wait(done, 0u, a.err, ERR_WAIT_FULL);
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcN) : "memory");
     }

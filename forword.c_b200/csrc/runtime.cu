@@ -1290,8 +1290,10 @@ static bool launch_tc_gemm(const void *w, size_t w_bytes, uint32_t type, const v
     int dev = 0;
     CK(cudaGetDevice(&dev));
     if (dev < 64 && !attr_set[dev]) {
-        CK(cudaFuncSetAttribute((const void *)gemm_q4_0_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        CK(cudaFuncSetAttribute((const void *)gemm_q4_0_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)kTcSmem));
+        CK(cudaFuncSetAttribute((const void *)gemm_q4_0_tc_kernel<false>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem));
         attr_set[dev] = true;
     }
     TcArgs a{};
@@ -1306,7 +1308,10 @@ static bool launch_tc_gemm(const void *w, size_t w_bytes, uint32_t type, const v
     a.mode = mode;
     a.err = err;
     const dim3 grid((unsigned)((N + kTcN - 1) / kTcN), (unsigned)((M + kTcM - 1) / kTcM));
-    gemm_q4_0_tc_kernel<<<grid, kTcThreads, kTcSmem, st>>>(a);
+    if (row_bytes % 16 == 0 && (uintptr_t)w % 16 == 0)  // 16-byte weight loads
+        gemm_q4_0_tc_kernel<true><<<grid, kTcThreads, kTcSmem, st>>>(a);
+    else
+        gemm_q4_0_tc_kernel<false><<<grid, kTcThreads, kTcSmem, st>>>(a);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) { set_err(std::string("quant_gemm launch: ") + cudaGetErrorString(e)); return false; }
     return true;
