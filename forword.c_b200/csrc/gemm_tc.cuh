@@ -10,25 +10,32 @@
 //
 // Tile: 128 tokens (TMEM lanes) x 128 weight rows (TMEM columns) per CTA, K
 // in steps of 64 (two Q4_0 blocks) through a ring of kTcStages shared-memory
-// stages, two CTAs per SM.  Warp-specialised: four producer warps fill a
-// stage -- thread t copies token row t's 64 activations and dequantises
-// weight row t's two blocks, (q - 8) * d rounded once to fp16 with half2
-// arithmetic (bit-identical to rounding the exact fp32 product), into the
-// K-major 128-byte-swizzled layout the MMA reads -- and signal the stage's
-// `full` mbarrier; one thread of the fifth warp issues four
-// tcgen05.mma.kind::f16 (K = 16 each) per stage and commits them to the
-// stage's `empty` mbarrier, which the producers wait on before refilling it.
-// Producers fetch the next stage's activation row and the next 256-wide K
-// chunk of their weight row (144 bytes, 16-byte loads when the rows allow)
-// one step ahead.  After the last MMA a commit to `done` releases the
-// epilogue: the producer warps read the accumulator with tcgen05.ld (warp w
-// owns TMEM lanes 32w..32w+31) and store, or add into, Y.
+// stages, two CTAs per SM.  Warp-specialised, six warps:
+//  * warps 0-3 (producers): thread t dequantises weight row t's two blocks
+//    of the step, (q - 8) * d rounded once to fp16 with half2 arithmetic
+//    (bit-identical to rounding the exact fp32 product), into the K-major
+//    128-byte-swizzled B tile, and the warp arrives on the stage's `full`
+//    mbarrier.  The weight row streams through registers a 256-wide K chunk
+//    (144 bytes, 16-byte loads when the rows allow) ahead;
+//  * warp 5, one thread: the stage's activation tile (128 tokens x 64 fp16)
+//    by TMA (cp.async.bulk.tensor, 2-D map with the 128-byte swizzle, no
+//    multicast; rows past M read as zeros) onto the stage's `afull`
+//    mbarrier, as far ahead as the ring allows;
+//  * warp 4, one thread: waits for both barriers, issues four
+//    tcgen05.mma.kind::f16 (K = 16 each) and commits them to the stage's
+//    `empty` mbarrier, which the producers and the TMA thread wait on before
+//    refilling the stage.
+// After the last MMA a commit to `done` releases the epilogue: the producer
+// warps read the accumulator with tcgen05.ld (warp w owns TMEM lanes
+// 32w..32w+31) and store, or add into, Y.
 //
 // Numerics: fp16 weights carry (q - 8) * d to 11 significant bits and fp16
 // activations x to 11 bits; products and sums are fp32.  Every wait is
 // bounded and sets an error bit; the MMA thread always makes the final
 // commit, so the TMEM columns are released only after every issued MMA.
 #pragma once
+#include <cuda.h>  // CUtensorMap
+
 #include "common.cuh"
 
 namespace fwb {
@@ -37,14 +44,15 @@ constexpr uint32_t kTcM = 128;        // tokens per tile
 constexpr uint32_t kTcN = 128;        // weight rows per tile
 constexpr uint32_t kTcK = 64;         // K per stage
 constexpr uint32_t kTcStages = 3;     // ring depth (two CTAs per SM)
-constexpr uint32_t kTcProducers = 128;  // four producer warps; a fifth issues the MMAs
-constexpr uint32_t kTcThreads = kTcProducers + 32;
+constexpr uint32_t kTcProducers = 128;  // four producer warps; a fifth issues the MMAs, a sixth the TMA
+constexpr uint32_t kTcThreads = kTcProducers + 64;
 constexpr uint32_t kTcTileBytes = 128 * 128;  // 128 rows of 64 fp16 (128 B)
 constexpr uint32_t kTcSmem = kTcStages * 2 * kTcTileBytes + 1024 + 256;  // stages x (A, B), alignment, barriers
 
 enum TcMode : uint32_t { TC_STORE = 0, TC_ADD = 1 };
 
 struct TcArgs {
+    CUtensorMap xmap;     // the activations as a 2-D tensor map: box 64 x 128, 128-byte swizzle
     const uint8_t *w;     // Q4_0 rows [N][K/32 blocks]
     uint32_t row_bytes;   // K/32 * 18
     const __half *x;      // [M][K] fp16, row-major
@@ -147,17 +155,15 @@ __device__ __forceinline__ void tc_dequant_row(const uint32_t (&w)[9], uint8_t *
     }
 }
 
-// This producer thread's activation row of K step k0 (64 fp16; zeros
-// outside M).
-__device__ __forceinline__ void tc_fetch_a(const TcArgs &a, uint32_t m, uint32_t k0, uint4 (&r)[8]) {
-    if (m < a.M) {
-        const uint4 *src = reinterpret_cast<const uint4 *>(a.x + (size_t)m * a.K + k0);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) r[i] = __ldg(src + i);
-    } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) r[i] = make_uint4(0u, 0u, 0u, 0u);
-    }
+// One activation tile (64 K values x 128 tokens from (k0, m0)) by TMA into
+// a 1024-byte-aligned stage, completing on `bar`.
+__device__ __forceinline__ void tc_tma_x(uint8_t *dst, const CUtensorMap *map, uint32_t k0, uint32_t m0,
+                                         uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(k0), "r"(m0), "r"(smem_u32(bar))
+        : "memory");
 }
 
 // 4 K steps (one 256-wide chunk, 36 words) of this producer's weight row
@@ -187,7 +193,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) gemm_q4_0_tc_kernel(const __gri
     const uint32_t base = (smem_u32(tc_smem_raw) + 1023u) & ~1023u;
     uint8_t *smem = tc_smem_raw + (base - smem_u32(tc_smem_raw));
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + kTcStages * 2 * kTcTileBytes);
-    uint64_t *empty = full + kTcStages, *done = empty + kTcStages;
+    uint64_t *afull = full + kTcStages, *empty = afull + kTcStages, *done = empty + kTcStages;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t n0 = blockIdx.x * kTcN, m0 = blockIdx.y * kTcM;
@@ -196,6 +202,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) gemm_q4_0_tc_kernel(const __gri
     if (tid == 0) {
         for (uint32_t s = 0; s < kTcStages; ++s) {
             mbar_init(&full[s], kTcProducers / 32);
+            mbar_init(&afull[s], 1);
             mbar_init(&empty[s], 1);
         }
         mbar_init(done, 1);
@@ -219,7 +226,11 @@ __global__ void __launch_bounds__(kTcThreads, 2) gemm_q4_0_tc_kernel(const __gri
             uint32_t i = 0;
             for (; i < steps; ++i) {
                 const uint32_t s = i % kTcStages;
-                if (!mbar_wait(&full[s], (i / kTcStages) & 1u, a.err, ERR_WAIT_FULL)) { ok = false; break; }
+                if (!mbar_wait(&full[s], (i / kTcStages) & 1u, a.err, ERR_WAIT_FULL) ||
+                    !mbar_wait(&afull[s], (i / kTcStages) & 1u, a.err, ERR_WAIT_FULL)) {
+                    ok = false;
+                    break;
+                }
                 tc_fence_after();
                 uint8_t *sa = smem + s * 2u * kTcTileBytes, *sb = sa + kTcTileBytes;
                 const uint64_t da = tc_desc(smem_u32(sa)), db = tc_desc(smem_u32(sb));
@@ -231,15 +242,30 @@ __global__ void __launch_bounds__(kTcThreads, 2) gemm_q4_0_tc_kernel(const __gri
             tc_commit(done);  // covers every MMA issued above, also after a failed wait
         }
         __syncwarp();
-    } else {
-        // ---- producers: thread t fills token row t and weight row t of each stage
-        const uint32_t t = tid, m = m0 + t, n = n0 + t;
-        uint4 ar[8];
-        uint32_t wc[36];
-        if (steps) {
-            tc_fetch_a(a, m, 0, ar);
-            tc_fetch_w<V16>(a, n, 0, steps, wc);
+    } else if (warp == kTcProducers / 32 + 1) {
+        // ---- activation tiles by TMA: one thread
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&a.xmap)) : "memory");
+            uint32_t i = 0;
+            for (; i < steps; ++i) {
+                const uint32_t s = i % kTcStages;
+                if (i >= kTcStages &&
+                    !mbar_wait(&empty[s], ((i / kTcStages) - 1) & 1u, a.err, ERR_WAIT_EMPTY))
+                    break;
+                mbar_arrive_expect_tx(&afull[s], kTcTileBytes);
+                tc_tma_x(smem + s * 2u * kTcTileBytes, &a.xmap, i * kTcK, m0, &afull[s]);
+            }
+            // before the CTA may exit, the copies still in flight land (the
+            // MMA thread consumed every stage unless a wait failed)
+            for (uint32_t k = i > kTcStages ? i - kTcStages : 0; k < i; ++k)
+                mbar_wait(&afull[k % kTcStages], (k / kTcStages) & 1u, a.err, ERR_WAIT_DRAIN);
         }
+        __syncwarp();
+    } else {
+        // ---- producers: thread t fills weight row t of each stage
+        const uint32_t t = tid, n = n0 + t;
+        uint32_t wc[36];
+        if (steps) tc_fetch_w<V16>(a, n, 0, steps, wc);
         for (uint32_t c0 = 0; c0 < steps && ok; c0 += 4) {
             uint32_t wn[36];
             tc_fetch_w<V16>(a, n, c0 + 4, steps, wn);  // zeros past the last step
@@ -248,15 +274,11 @@ __global__ void __launch_bounds__(kTcThreads, 2) gemm_q4_0_tc_kernel(const __gri
                 const uint32_t i = c0 + j;
                 if (i < steps && ok) {
                     const uint32_t s = i % kTcStages;
-                    uint4 an[8];
-                    tc_fetch_a(a, m, i + 1 < steps ? (i + 1) * kTcK : i * kTcK, an);
                     if (i >= kTcStages)  // the MMAs that read this stage kTcStages steps ago are done
                         ok = __all_sync(0xffffffffu, mbar_wait(&empty[s], ((i / kTcStages) - 1) & 1u, a.err,
                                                                ERR_WAIT_EMPTY));
                     if (ok) {
-                        uint8_t *sa = smem + s * 2u * kTcTileBytes, *sb = sa + kTcTileBytes;
-#pragma unroll
-                        for (uint32_t q = 0; q < 8; ++q) *reinterpret_cast<uint4 *>(sa + tc_sw128(t, q)) = ar[q];
+                        uint8_t *sb = smem + s * 2u * kTcTileBytes + kTcTileBytes;
                         const uint32_t w9[9] = {wc[9 * j], wc[9 * j + 1], wc[9 * j + 2], wc[9 * j + 3], wc[9 * j + 4],
                                                 wc[9 * j + 5], wc[9 * j + 6], wc[9 * j + 7], wc[9 * j + 8]};
                         tc_dequant_row(w9, sb, t);
@@ -264,8 +286,6 @@ __global__ void __launch_bounds__(kTcThreads, 2) gemm_q4_0_tc_kernel(const __gri
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&full[s]);
                     }
-#pragma unroll
-                    for (uint32_t q = 0; q < 8; ++q) ar[q] = an[q];
                 }
             }
 #pragma unroll

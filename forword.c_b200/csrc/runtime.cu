@@ -1274,6 +1274,20 @@ int quant_device_status(void *stream) {
     return device_status(static_cast<cudaStream_t>(stream), "quant_device_status") ? 0 : -1;
 }
 
+// cuTensorMapEncodeTiled from the driver (through the runtime's entry-point
+// query, so the library does not link libcuda itself).
+static decltype(&cuTensorMapEncodeTiled) tensor_map_encoder() {
+    static decltype(&cuTensorMapEncodeTiled) fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<decltype(&cuTensorMapEncodeTiled)>(p);
+    }
+    return fn;
+}
+
 // Tensor-core dequant-GEMM launch (gemm_tc.cuh): Y[m][0..N) (row stride ldy)
 // = W X[m] for m < M, or += with TC_ADD.  Q4_0 with K a multiple of 64,
 // 4-byte-aligned weights and 16-byte-aligned fp16 activations only.
@@ -1297,6 +1311,17 @@ static bool launch_tc_gemm(const void *w, size_t w_bytes, uint32_t type, const v
         attr_set[dev] = true;
     }
     TcArgs a{};
+    {  // the activations [M][K] fp16 as a 2-D map: 64 x 128 boxes, 128-byte swizzle, zeros past M
+        const auto enc = tensor_map_encoder();
+        if (!enc) { set_err("quant_gemm: cuTensorMapEncodeTiled unavailable"); return false; }
+        const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
+        const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+        const cuuint32_t box[2] = {kTcK, kTcM}, estr[2] = {1, 1};
+        const CUresult r = enc(&a.xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(x), dims, strides, box,
+                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) { set_err("quant_gemm: activation tensor map rejected"); return false; }
+    }
     a.w = static_cast<const uint8_t *>(w);
     a.row_bytes = (uint32_t)row_bytes;
     a.x = static_cast<const __half *>(x);
