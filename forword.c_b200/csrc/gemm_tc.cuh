@@ -114,42 +114,43 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
     return *reinterpret_cast<const uint32_t *>(&h);
 }
 
-// Two fp16 values (q - 8) * d from the nibbles of bytes b and b + 1 of word
-// x (byte b = 0 or 2): (1024 + q) as fp16 bits, minus 1032, times d -- each
-// step exact but the last, which rounds the exact product once.
-template <bool HIGH>
-__device__ __forceinline__ uint32_t q4_pair(uint32_t x, uint32_t sel, __half2 d2) {
-    uint32_t p = __byte_perm(x, 0u, sel);  // byte b -> byte 0, byte b+1 -> byte 2
-    if (HIGH) p >>= 4;
-    p = (p & 0x000F000Fu) | 0x64006400u;
-    const __half2 v = __hmul2(__hsub2(*reinterpret_cast<const __half2 *>(&p), __float2half2_rn(1032.0f)), d2);
+// (q - 8) * d for a pair of fp16 values whose bits are 0x6400 | q (that is,
+// 1024 + q): minus 1032, then times d -- each step exact but the last,
+// which rounds the exact product once.
+__device__ __forceinline__ uint32_t q4_scale(uint32_t p, __half2 d2) {
+    const __half2 k1032 = __halves2half2(__ushort_as_half((unsigned short)0x6408u),
+                                         __ushort_as_half((unsigned short)0x6408u));
+    const __half2 v = __hmul2(__hsub2(*reinterpret_cast<const __half2 *>(&p), k1032), d2);
     return *reinterpret_cast<const uint32_t *>(&v);
 }
 
 // Weight row t of one K step (two Q4_0 blocks in 9 words, the first block's
 // scale in the low half of w[0], the second's in the high half of w[4]) into
-// the swizzled B tile: 8 chunks of 8 fp16.
+// the swizzled B tile: 8 chunks of 8 fp16.  Element j < 16 of a block is the
+// low nibble of quant byte j, element 16 + j the high nibble; a word of
+// nibbles (4 bytes) becomes two fp16 pairs 0x64qq by one byte permutation
+// each.
 __device__ __forceinline__ void tc_dequant_row(const uint32_t (&w)[9], uint8_t *sb, uint32_t t) {
 #pragma unroll
     for (uint32_t blk = 0; blk < 2; ++blk) {
         const uint32_t dbits = blk ? (w[4] >> 16) : (w[0] & 0xffffu);
         const __half dh = __ushort_as_half((unsigned short)dbits);
         const __half2 d2 = __halves2half2(dh, dh);
-        uint32_t qs[4];
+        uint32_t nib[8];  // [0..3]: low nibbles of quant words 0..3, [4..7]: high nibbles
 #pragma unroll
-        for (int i = 0; i < 4; ++i) qs[i] = blk ? w[5 + i] : __funnelshift_r(w[i], w[i + 1], 16);
-        // element j < 16: low nibble of byte j; element 16 + j: high nibble
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t q = blk ? w[5 + i] : __funnelshift_r(w[i], w[i + 1], 16);
+            nib[i] = q & 0x0F0F0F0Fu;
+            nib[4 + i] = (q >> 4) & 0x0F0F0F0Fu;
+        }
 #pragma unroll
-        for (uint32_t c = 0; c < 4; ++c) {
-            const uint32_t x0 = qs[(c & 1) * 2], x1 = qs[(c & 1) * 2 + 1];
+        for (uint32_t c = 0; c < 4; ++c) {  // chunk c: elements 8c .. 8c + 7 = nibble words 2c, 2c + 1
+            const uint32_t x0 = nib[2 * c], x1 = nib[2 * c + 1];
             uint4 o;
-            if (c < 2) {
-                o.x = q4_pair<false>(x0, 0x4140u, d2); o.y = q4_pair<false>(x0, 0x4342u, d2);
-                o.z = q4_pair<false>(x1, 0x4140u, d2); o.w = q4_pair<false>(x1, 0x4342u, d2);
-            } else {
-                o.x = q4_pair<true>(x0, 0x4140u, d2); o.y = q4_pair<true>(x0, 0x4342u, d2);
-                o.z = q4_pair<true>(x1, 0x4140u, d2); o.w = q4_pair<true>(x1, 0x4342u, d2);
-            }
+            o.x = q4_scale(__byte_perm(x0, 0x64646464u, 0x4140u), d2);
+            o.y = q4_scale(__byte_perm(x0, 0x64646464u, 0x4342u), d2);
+            o.z = q4_scale(__byte_perm(x1, 0x64646464u, 0x4140u), d2);
+            o.w = q4_scale(__byte_perm(x1, 0x64646464u, 0x4342u), d2);
             *reinterpret_cast<uint4 *>(sb + tc_sw128(t, blk * 4 + c)) = o;
         }
     }

@@ -46,16 +46,40 @@ __device__ __forceinline__ float pf_block_max(float v, float *red) {
     return t;
 }
 
-// out[t] = fp16(x[t] * w * (1 / sqrtf(mean(x[t]^2) + eps))), one block per token
+// out[t] = fp16(x[t] * w * (1 / sqrtf(mean(x[t]^2) + eps))), one block per
+// token.  n % 4 == 0 and n <= 16 * 4 * blockDim.x: the row is read once, as
+// float4, and kept in registers for the scaling pass.
+constexpr int kPfNormVec = 16;  // float4 per thread at most
 __global__ void pf_rmsnorm_f16_kernel(const float *x, const float *w, float eps, uint32_t n, __half *out) {
     __shared__ float red[32];
-    const float *xr = x + (size_t)blockIdx.x * n;
+    const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)blockIdx.x * n);
+    const float4 *wr = reinterpret_cast<const float4 *>(w);
+    const uint32_t n4 = n / 4;
+    float4 v[kPfNormVec];
     float ss = 0.f;
-    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+#pragma unroll
+    for (int k = 0; k < kPfNormVec; ++k) {
+        const uint32_t i = threadIdx.x + k * blockDim.x;
+        v[k] = i < n4 ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int k = 0; k < kPfNormVec; ++k)
+        ss = fmaf(v[k].w, v[k].w, fmaf(v[k].z, v[k].z, fmaf(v[k].y, v[k].y, fmaf(v[k].x, v[k].x, ss))));
     ss = pf_block_sum(ss, red);
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
-    __half *o = out + (size_t)blockIdx.x * n;
-    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) o[i] = __float2half_rn(__fmul_rn(__fmul_rn(xr[i], w[i]), scale));
+    uint2 *o = reinterpret_cast<uint2 *>(out + (size_t)blockIdx.x * n);
+#pragma unroll
+    for (int k = 0; k < kPfNormVec; ++k) {
+        const uint32_t i = threadIdx.x + k * blockDim.x;
+        if (i < n4) {
+            const float4 g = __ldg(wr + i);
+            const __half2 a = __floats2half2_rn(__fmul_rn(__fmul_rn(v[k].x, g.x), scale),
+                                                __fmul_rn(__fmul_rn(v[k].y, g.y), scale));
+            const __half2 b = __floats2half2_rn(__fmul_rn(__fmul_rn(v[k].z, g.z), scale),
+                                                __fmul_rn(__fmul_rn(v[k].w, g.w), scale));
+            o[i] = make_uint2(*reinterpret_cast<const uint32_t *>(&a), *reinterpret_cast<const uint32_t *>(&b));
+        }
+    }
 }
 
 // Rows [q | k | v] of the QKV GEMM output for token t at position p0 + t: RoPE
@@ -223,12 +247,193 @@ __global__ void pf_attn_gqa_kernel(const float *qf, const float *kcache, const f
     }
 }
 
-// h = fp16(silu(gate) * up) (ffn.c:17-25, 90-106)
+// Causal attention of the prompt, tiled (flash form) on the CUDA cores in
+// fp32.  A block owns R query rows -- QT = R / GQ consecutive tokens x the
+// GQ query heads of one KV head (row r: token r / GQ, head r % GQ) -- and
+// walks the positions 0 .. p0 + (its last token) in tiles of KT K / V rows
+// staged in shared memory (rows padded by 4 floats: conflict-free 16-byte
+// reads).  Per tile: scores S = q.k * scale (attention.c:150-154; each
+// thread SR rows x SK positions, dot products in dimension order), causal
+// mask, online softmax (running row maximum and sum, expf as
+// attention.c:18-33), O += P V (each thread R*16/threads rows x HD/16
+// dimensions).
+// The output is O / l, rounded to fp16 for the o-proj GEMM.  Grid
+// (ceil(nqt/2), n_kv): block b takes query tiles b and nqt-1-b, so every
+// block walks about the same number of key tiles.
+constexpr int kPfRows = 64, kPfKeys = 64, kPfSR = 4, kPfSK = 4, kPfThreads = 256;
+template <int HD>
+__host__ __device__ constexpr uint32_t pf_flash_smem() {
+    return (uint32_t)((kPfRows + 2 * kPfKeys) * (HD + 4) + kPfRows * kPfKeys + 2 * kPfRows) * 4u;
+}
+
+template <int HD, int GQ>
+__global__ void __launch_bounds__(kPfThreads) pf_flash_kernel(const float *qf, const float *kcache,
+                                                              const float *vcache, uint32_t T, uint32_t p0,
+                                                              uint32_t n_head, uint32_t kv_ctx, float scale,
+                                                              __half *out) {
+    static_assert(HD == 64 || HD == 128, "head_dim");
+    constexpr int R = kPfRows, KT = kPfKeys, LD = HD + 4, QT = R / GQ, DV = HD / 16;
+    constexpr int SR = kPfSR, SK = kPfSK, NC = KT / SK, RO = R * 16 / kPfThreads;
+    static_assert((R / SR) * NC == kPfThreads && NC <= 32 && R % GQ == 0 && RO >= 1 && RO * kPfThreads == R * 16,
+                  "thread mapping");
+    extern __shared__ float4 pf_flash_raw[];
+    float *Qs = reinterpret_cast<float *>(pf_flash_raw);
+    float *Ks = Qs + R * LD, *Vs = Ks + KT * LD, *Ps = Vs + KT * LD;  // Ps [R][KT]
+    float *alpha_s = Ps + R * KT, *linv_s = alpha_s + R;
+    const uint32_t tid = threadIdx.x, kvh = blockIdx.y;
+    const uint32_t nq = n_head * HD, nqt = (T + QT - 1) / QT;
+    const float *kb = kcache + (size_t)kvh * kv_ctx * HD, *vb = vcache + (size_t)kvh * kv_ctx * HD;
+    // score mapping: rows SR tr + a; positions tc + NC j (the NC lanes of a row group are adjacent)
+    const uint32_t tr = tid / NC, tc = tid % NC;
+    // output mapping: rows RO ro + r; dimensions 4 dg .. 4 dg + 3 (and 64 + 4 dg .. for HD 128)
+    const uint32_t ro = tid >> 4, dg = tid & 15;
+
+    for (uint32_t pass = 0; pass < 2; ++pass) {
+        const uint32_t qt = pass == 0 ? blockIdx.x : nqt - 1 - blockIdx.x;
+        if (pass == 1 && qt <= blockIdx.x) break;  // odd count: the middle tile once
+        const uint32_t t0 = qt * QT;
+        __syncthreads();  // the previous pass's reads of Qs are done
+        // query rows (rows of tokens >= T are zeros and produce no output)
+        for (uint32_t i = tid; i < (uint32_t)(R * HD / 4); i += kPfThreads) {
+            const uint32_t r = i / (HD / 4), c4 = i % (HD / 4), tq = t0 + r / GQ;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (tq < T)
+                v = *reinterpret_cast<const float4 *>(qf + (size_t)tq * nq + (size_t)(kvh * GQ + r % GQ) * HD + 4 * c4);
+            *reinterpret_cast<float4 *>(Qs + r * LD + 4 * c4) = v;
+        }
+        float m[SR], l[SR];
+#pragma unroll
+        for (int a = 0; a < SR; ++a) { m[a] = -INFINITY; l[a] = 0.f; }
+        float o[RO][DV];
+#pragma unroll
+        for (int r = 0; r < RO; ++r)
+#pragma unroll
+            for (int d = 0; d < DV; ++d) o[r][d] = 0.f;
+        const uint32_t t_last = min(T, t0 + QT) - 1;
+        const uint32_t n_keys = p0 + t_last + 1;
+        for (uint32_t k0 = 0; k0 < n_keys; k0 += KT) {
+            __syncthreads();  // previous tile's K / V / P reads are done
+            for (uint32_t i = tid; i < (uint32_t)(KT * HD / 4); i += kPfThreads) {
+                const uint32_t r = i / (HD / 4), c4 = i % (HD / 4), j = k0 + r;
+                float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+                if (j < n_keys) {
+                    kv = *reinterpret_cast<const float4 *>(kb + (size_t)j * HD + 4 * c4);
+                    vv = *reinterpret_cast<const float4 *>(vb + (size_t)j * HD + 4 * c4);
+                }
+                *reinterpret_cast<float4 *>(Ks + r * LD + 4 * c4) = kv;
+                *reinterpret_cast<float4 *>(Vs + r * LD + 4 * c4) = vv;
+            }
+            __syncthreads();
+            float sc[SR][SK];
+#pragma unroll
+            for (int a = 0; a < SR; ++a)
+#pragma unroll
+                for (int j = 0; j < SK; ++j) sc[a][j] = 0.f;
+#pragma unroll 2
+            for (int d = 0; d < HD; d += 4) {
+                float4 q[SR];
+#pragma unroll
+                for (int a = 0; a < SR; ++a) q[a] = *reinterpret_cast<const float4 *>(Qs + (SR * tr + a) * LD + d);
+#pragma unroll
+                for (int j = 0; j < SK; ++j) {
+                    const float4 k = *reinterpret_cast<const float4 *>(Ks + (tc + NC * j) * LD + d);
+#pragma unroll
+                    for (int a = 0; a < SR; ++a)
+                        sc[a][j] = fmaf(q[a].w, k.w, fmaf(q[a].z, k.z, fmaf(q[a].y, k.y, fmaf(q[a].x, k.x, sc[a][j]))));
+                }
+            }
+            // causal mask, online softmax (the NC lanes of a row group share its rows)
+#pragma unroll
+            for (int a = 0; a < SR; ++a) {
+                const uint32_t pos = p0 + t0 + (SR * tr + a) / GQ;
+                float mx = -INFINITY;
+#pragma unroll
+                for (int j = 0; j < SK; ++j) {
+                    const uint32_t key = k0 + tc + NC * j;
+                    sc[a][j] = key <= pos ? __fmul_rn(sc[a][j], scale) : -INFINITY;
+                    mx = fmaxf(mx, sc[a][j]);
+                }
+#pragma unroll
+                for (int off = 1; off < NC; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+                const float mn = fmaxf(m[a], mx);
+                const float al = mn == -INFINITY ? 1.f : expf(m[a] - mn);
+                float sum = 0.f;
+#pragma unroll
+                for (int j = 0; j < SK; ++j) {
+                    const float e = sc[a][j] == -INFINITY ? 0.f : expf(sc[a][j] - mn);
+                    Ps[(SR * tr + a) * KT + tc + NC * j] = e;
+                    sum += e;
+                }
+#pragma unroll
+                for (int off = 1; off < NC; off <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+                l[a] = fmaf(l[a], al, sum);
+                m[a] = mn;
+                if (tc == 0) alpha_s[SR * tr + a] = al;
+            }
+            __syncthreads();
+            // O = O * alpha + P V for rows RO ro + r
+#pragma unroll
+            for (int r = 0; r < RO; ++r) {
+                const float al = alpha_s[RO * ro + r];
+#pragma unroll
+                for (int d = 0; d < DV; ++d) o[r][d] *= al;
+            }
+            const uint32_t kn = min((uint32_t)KT, n_keys - k0);
+#pragma unroll 4
+            for (uint32_t j = 0; j < kn; ++j) {
+                const float4 v0 = *reinterpret_cast<const float4 *>(Vs + j * LD + 4 * dg);
+                float4 v1 = v0;
+                if (DV == 8) v1 = *reinterpret_cast<const float4 *>(Vs + j * LD + 64 + 4 * dg);
+#pragma unroll
+                for (int r = 0; r < RO; ++r) {
+                    const float p = Ps[(RO * ro + r) * KT + j];
+                    o[r][0] = fmaf(p, v0.x, o[r][0]);
+                    o[r][1] = fmaf(p, v0.y, o[r][1]);
+                    o[r][2] = fmaf(p, v0.z, o[r][2]);
+                    o[r][3] = fmaf(p, v0.w, o[r][3]);
+                    if (DV == 8) {
+                        o[r][DV - 4] = fmaf(p, v1.x, o[r][DV - 4]);
+                        o[r][DV - 3] = fmaf(p, v1.y, o[r][DV - 3]);
+                        o[r][DV - 2] = fmaf(p, v1.z, o[r][DV - 2]);
+                        o[r][DV - 1] = fmaf(p, v1.w, o[r][DV - 1]);
+                    }
+                }
+            }
+        }
+        if (tc == 0)
+#pragma unroll
+            for (int a = 0; a < SR; ++a) linv_s[SR * tr + a] = l[a];
+        __syncthreads();
+#pragma unroll
+        for (int r = 0; r < RO; ++r) {
+            const uint32_t row = RO * ro + r, tq = t0 + row / GQ;
+            if (tq >= T) continue;
+            const float L = linv_s[row];
+            __half *dst = out + (size_t)tq * nq + (size_t)(kvh * GQ + row % GQ) * HD;
+#pragma unroll
+            for (int d = 0; d < DV; ++d) {
+                const uint32_t dim = d < 4 ? 4 * dg + d : 64 + 4 * dg + (d - 4);
+                dst[dim] = __float2half_rn(__fdiv_rn(o[r][d], L));
+            }
+        }
+    }
+}
+
+// h = fp16(silu(gate) * up) (ffn.c:17-25, 90-106); n % 4 == 0, four values
+// per thread and step (float4 loads, one 8-byte store)
+__device__ __forceinline__ float pf_silu_mul(float v, float u) {
+    const float sig = v >= 0.0f ? __fdiv_rn(1.0f, 1.0f + expf(-v)) : __fdiv_rn(expf(v), 1.0f + expf(v));
+    return __fmul_rn(__fmul_rn(v, sig), u);
+}
 __global__ void pf_swiglu_kernel(const float *g, const float *u, size_t n, __half *h) {
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
-        const float v = g[i];
-        const float sig = v >= 0.0f ? __fdiv_rn(1.0f, 1.0f + expf(-v)) : __fdiv_rn(expf(v), 1.0f + expf(v));
-        h[i] = __float2half_rn(__fmul_rn(__fmul_rn(v, sig), u[i]));
+    const size_t n4 = n / 4;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+        const float4 a = __ldcs(reinterpret_cast<const float4 *>(g) + i);
+        const float4 b = __ldcs(reinterpret_cast<const float4 *>(u) + i);
+        const __half2 lo = __floats2half2_rn(pf_silu_mul(a.x, b.x), pf_silu_mul(a.y, b.y));
+        const __half2 hi = __floats2half2_rn(pf_silu_mul(a.z, b.z), pf_silu_mul(a.w, b.w));
+        reinterpret_cast<uint2 *>(h)[i] = make_uint2(*reinterpret_cast<const uint32_t *>(&lo),
+                                                     *reinterpret_cast<const uint32_t *>(&hi));
     }
 }
 

@@ -1509,6 +1509,7 @@ int fwb_model_kernels_per_step(const fwb_model_t *m) {
 static bool prefill_eligible(const fwb_model *m) {
     const ModelConfig &c = m->cfg;
     if (m->world != 1 || c.head_dim > 128 || c.head_dim % 4 || c.n_head % c.n_head_kv) return false;
+    if (c.n_embd > (uint32_t)kPfNormVec * 4 * 256) return false;  // the RMSNorm kernel's register row
     for (const LayerW &w : m->layers)
         if (w.v.p) return false;  // a v matrix of another type than q / k
     for (const LayerW &w : m->layers)
@@ -1534,13 +1535,37 @@ static bool prefill_alloc(fwb_model *m) {
     return true;
 }
 
-// Prompt attention: all query heads of a KV head per block when their scores
-// fit in shared memory (GQ 1, 2, 4 or 8), else one block per query head.
+// Prompt attention: the tiled flash kernel for head_dim 64 / 128 and groups
+// of 1, 2, 4 or 8 query heads; otherwise all query heads of a KV head per
+// block when their scores fit in shared memory, else one block per query head.
+static bool launch_pf_flash(fwb_model *m, const void *fn, uint32_t smem, uint32_t gq, const float *kc,
+                            const float *vc, uint32_t T, uint32_t p0, float scale, cudaStream_t st) {
+    CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    const uint32_t H = m->cfg.n_head, QT = kPfRows / gq, nqt = (T + QT - 1) / QT;
+    void *args[] = {(void *)&m->pf_q, (void *)&kc, (void *)&vc, (void *)&T, (void *)&p0,
+                    (void *)&H, (void *)&m->kv_ctx, (void *)&scale, (void *)&m->pf_a16};
+    CK(cudaLaunchKernel(fn, dim3((nqt + 1) / 2, m->cfg.n_head_kv), dim3(kPfThreads), args, smem, st));
+    return true;
+}
+
 static bool launch_pf_attn(fwb_model *m, const float *kc, const float *vc, uint32_t T, uint32_t p0,
                            size_t att_smem, cudaStream_t st) {
     const ModelConfig &c = m->cfg;
     const uint32_t H = c.n_head, KV = c.n_head_kv, hd = c.head_dim, gq = H / KV;
     const float scale = 1.0f / sqrtf((float)hd);
+    if (hd == 128 || hd == 64) {
+        switch (gq * 1000 + hd) {
+        case 1128: return launch_pf_flash(m, (const void *)pf_flash_kernel<128, 1>, pf_flash_smem<128>(), 1, kc, vc, T, p0, scale, st);
+        case 2128: return launch_pf_flash(m, (const void *)pf_flash_kernel<128, 2>, pf_flash_smem<128>(), 2, kc, vc, T, p0, scale, st);
+        case 4128: return launch_pf_flash(m, (const void *)pf_flash_kernel<128, 4>, pf_flash_smem<128>(), 4, kc, vc, T, p0, scale, st);
+        case 8128: return launch_pf_flash(m, (const void *)pf_flash_kernel<128, 8>, pf_flash_smem<128>(), 8, kc, vc, T, p0, scale, st);
+        case 1064: return launch_pf_flash(m, (const void *)pf_flash_kernel<64, 1>, pf_flash_smem<64>(), 1, kc, vc, T, p0, scale, st);
+        case 2064: return launch_pf_flash(m, (const void *)pf_flash_kernel<64, 2>, pf_flash_smem<64>(), 2, kc, vc, T, p0, scale, st);
+        case 4064: return launch_pf_flash(m, (const void *)pf_flash_kernel<64, 4>, pf_flash_smem<64>(), 4, kc, vc, T, p0, scale, st);
+        case 8064: return launch_pf_flash(m, (const void *)pf_flash_kernel<64, 8>, pf_flash_smem<64>(), 8, kc, vc, T, p0, scale, st);
+        default: break;
+        }
+    }
     const size_t smem_g = att_smem * gq;
     auto run = [&](const void *fn) -> bool {
         if (smem_g > 48 * 1024)
@@ -1598,7 +1623,7 @@ static bool prefill_chunk(fwb_model *m, const uint32_t *tokens, uint32_t T, uint
             !launch_tc_gemm(w.up.p, (size_t)w.up.rows * w.up.row_bytes, 2, m->pf_h16, m->pf_u, E, F, T, F, TC_STORE,
                             st, m->err))
             return false;
-        pf_swiglu_kernel<<<std::min<size_t>(4096, ((size_t)T * F + 255) / 256), 256, 0, st>>>(
+        pf_swiglu_kernel<<<std::min<size_t>(4 * 148, ((size_t)T * F / 4 + 255) / 256), 256, 0, st>>>(
             m->pf_g, m->pf_u, (size_t)T * F, m->pf_h16);
         if (!launch_tc_gemm(w.down.p, (size_t)w.down.rows * w.down.row_bytes, 2, m->pf_h16, m->pf_x, F, E, T, E,
                             TC_ADD, st, m->err))
