@@ -462,7 +462,8 @@ def run_b200(args) -> None:
             "metric": METRIC, "value": K / (ms / 1e3), "unit": UNIT, "n_gpus": world,
             "steps": K, "warmup": W, "ms_per_step": ms / K, "higher_is_better": True,
             "scaling": "strong" if wl.tp else "weak", "vs_baseline": None,
-            "dtype": "q4_0 weights x 16-bit block fixed-point activations (dp4a), fp32 accumulate",
+            "dtype": "q4_0 weights x 24-bit block fixed-point activations (three dp4a byte planes, exact "
+                     "integer block sums), fp32 accumulate",
             "data": "synthetic (seeded random weights and prompt)",
             "config": wl.config(world, K, W, kv_ctx),
             "roofline": {

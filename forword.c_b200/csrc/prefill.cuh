@@ -10,6 +10,7 @@
 // GEMM are rounded to fp16; everything else is fp32.
 #pragma once
 #include "common.cuh"
+#include "gemm_tc.cuh"
 
 namespace fwb {
 
@@ -416,6 +417,264 @@ __global__ void __launch_bounds__(kPfThreads) pf_flash_kernel(const float *qf, c
                 dst[dim] = __float2half_rn(__fdiv_rn(o[r][d], L));
             }
         }
+    }
+}
+
+// Causal attention of the prompt on the tensor cores (head_dim 128).  A
+// block owns 128 query rows -- 128 / GQ consecutive tokens x the GQ query
+// heads of one KV head (row r: token r / GQ, head r % GQ) -- one row per
+// thread and TMEM lane, and walks the positions 0 .. p0 + (its last token)
+// in tiles of 64.  Per tile:
+//  * the K tile (64 x 128) and the V tile are rounded to fp16 into shared
+//    memory in the K-major 128-byte-swizzled layout (V transposed: dims x
+//    positions), q once per block the same way (two 64-dim halves);
+//  * one thread issues S = q k^T as tcgen05.mma.kind::f16 (M 128, N 64,
+//    K 8 x 16; fp32 in TMEM columns 0..63) and commits to an mbarrier;
+//  * each thread reads its row's 64 scores (tcgen05.ld), scales by
+//    1/sqrt(head_dim) (attention.c:150-154), masks the causal future, and
+//    updates its running maximum and sum (online softmax, expf as
+//    attention.c:18-33).  The output accumulator is rescaled in TMEM only
+//    when the row maximum grows by more than 5 (a factor e^5 keeps the
+//    probabilities of the tile within fp16), so the reference point m_used
+//    changes rarely; p = expf(s - m_used) is rounded to fp16 into the P tile
+//    and the row sum adds those rounded values;
+//  * one thread issues O += P V (M 128, N 128, K 4 x 16; TMEM columns
+//    128..255) and commits to the second mbarrier, which the next tile waits
+//    on before it overwrites K, V and P.
+// The output is O / l rounded to fp16 for the o-proj GEMM.  Every wait is
+// bounded; a failed wait sets the error word, the block stops issuing MMAs,
+// and a final commit is waited for before TMEM is released.
+constexpr uint32_t kAtRows = 128, kAtKeys = 64, kAtHd = 128, kAtThreads = 128;
+constexpr uint32_t kAtQBytes = kAtRows * kAtHd * 2;   // two 64-dim halves of 16 KB
+constexpr uint32_t kAtKBytes = kAtKeys * kAtHd * 2;   // two halves of 8 KB
+constexpr uint32_t kAtVBytes = kAtHd * kAtKeys * 2;   // 128 dims x 64 positions
+constexpr uint32_t kAtPBytes = kAtRows * kAtKeys * 2; // 128 rows x 64 positions
+constexpr uint32_t kAtSmem = kAtQBytes + kAtKBytes + kAtVBytes + kAtPBytes + 1024 + 128;
+constexpr float kAtRescale = 5.0f;
+
+__device__ __forceinline__ void at_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+        : "memory");
+}
+// kind::f16 instruction descriptor: fp32 accumulator, fp16 A and B, both
+// K-major, M 128, N n
+__host__ __device__ constexpr uint32_t at_idesc(uint32_t n) {
+    return (1u << 4) | ((n >> 3) << 17) | ((128u >> 4) << 24);
+}
+__device__ __forceinline__ void at_st32(uint32_t taddr, const float (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+        "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+        "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+        "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+        "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+        "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+        "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+        "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+        "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+        "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+template <int GQ>
+__global__ void __launch_bounds__(kAtThreads) pf_attn_tc_kernel(const float *qf, const float *kcache,
+                                                                const float *vcache, uint32_t T, uint32_t p0,
+                                                                uint32_t n_head, uint32_t kv_ctx, float scale,
+                                                                __half *out, uint32_t *err) {
+    constexpr uint32_t QT = kAtRows / GQ, HD = kAtHd;
+    extern __shared__ uint8_t at_smem_raw[];
+    const uint32_t base = (smem_u32(at_smem_raw) + 1023u) & ~1023u;
+    uint8_t *sm = at_smem_raw + (base - smem_u32(at_smem_raw));
+    uint8_t *Qs = sm, *Ks = Qs + kAtQBytes, *Vt = Ks + kAtKBytes, *Ps = Vt + kAtVBytes;
+    uint64_t *bar = reinterpret_cast<uint64_t *>(Ps + kAtPBytes);  // [0] S done, [1] PV done, [2] final
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar + 3);
+    uint32_t *bad = tmem_slot + 1;
+    const uint32_t tid = threadIdx.x, warp = tid >> 5, kvh = blockIdx.y;
+    const uint32_t nq = n_head * HD, nqt = (T + QT - 1) / QT;
+    const uint32_t qt = nqt - 1 - blockIdx.x;  // the longest key ranges start first
+    const uint32_t t0 = qt * QT;
+    const float *kb = kcache + (size_t)kvh * kv_ctx * HD, *vb = vcache + (size_t)kvh * kv_ctx * HD;
+
+    if (tid == 0) {
+        for (int i = 0; i < 3; ++i) mbar_init(&bar[i], 1);
+        *bad = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(256u)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    // this thread's query row -> fp16, swizzled (rows of tokens >= T are zeros)
+    const uint32_t r = tid, tq = t0 + r / GQ;
+    const bool live = tq < T;
+    {
+        const float *q = qf + (size_t)tq * nq + (size_t)(kvh * GQ + r % GQ) * HD;
+#pragma unroll 4
+        for (uint32_t c = 0; c < HD / 8; ++c) {
+            float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+            if (live) {
+                a = *reinterpret_cast<const float4 *>(q + 8 * c);
+                b = *reinterpret_cast<const float4 *>(q + 8 * c + 4);
+            }
+            uint4 o;
+            o.x = pack_h2(a.x, a.y); o.y = pack_h2(a.z, a.w); o.z = pack_h2(b.x, b.y); o.w = pack_h2(b.z, b.w);
+            *reinterpret_cast<uint4 *>(Qs + (c / 8) * (kAtRows * 128) + tc_sw128(r, c % 8)) = o;
+        }
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot, tS = tmem, tO = tmem + 128;
+    const uint32_t lane_off = (warp * 32u) << 16;
+
+    const uint32_t t_last = min(T, t0 + QT) - 1;
+    const uint32_t n_keys = p0 + t_last + 1, n_tiles = (n_keys + kAtKeys - 1) / kAtKeys;
+    const uint32_t pos = p0 + tq;
+    float m_used = -INFINITY, l = 0.f;
+    for (uint32_t it = 0; it < n_tiles; ++it) {
+        const uint32_t k0 = it * kAtKeys;
+        // the previous tile's MMAs are done with K, V, P and O
+        if (it > 0 && !mbar_wait(&bar[1], (it - 1) & 1u, err, ERR_WAIT_FULL)) atomicExch(bad, 1u);
+        tc_fence_after();
+        {  // K and V rows of this tile -> fp16: thread t takes position t / 2, dims [64 (t & 1), +64)
+            const uint32_t j = tid >> 1, h = tid & 1, key = k0 + j;
+            const bool in = key < n_keys;
+            const float *kr = kb + (size_t)key * HD + 64 * h, *vr = vb + (size_t)key * HD + 64 * h;
+#pragma unroll 2
+            for (uint32_t c = 0; c < 8; ++c) {
+                float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a, va = a, vb4 = a;
+                if (in) {
+                    a = *reinterpret_cast<const float4 *>(kr + 8 * c);
+                    b = *reinterpret_cast<const float4 *>(kr + 8 * c + 4);
+                    va = *reinterpret_cast<const float4 *>(vr + 8 * c);
+                    vb4 = *reinterpret_cast<const float4 *>(vr + 8 * c + 4);
+                }
+                uint4 o;
+                o.x = pack_h2(a.x, a.y); o.y = pack_h2(a.z, a.w); o.z = pack_h2(b.x, b.y); o.w = pack_h2(b.z, b.w);
+                *reinterpret_cast<uint4 *>(Ks + h * (kAtKeys * 128) + tc_sw128(j, c)) = o;
+                // V transposed: row = dimension, K index = position j
+                const float vv[8] = {va.x, va.y, va.z, va.w, vb4.x, vb4.y, vb4.z, vb4.w};
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const uint32_t d = 64 * h + 8 * c + e;
+                    *reinterpret_cast<__half *>(Vt + tc_sw128(d, j >> 3) + 2 * (j & 7)) = __float2half_rn(vv[e]);
+                }
+            }
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        tc_fence_before();
+        __syncthreads();
+        const bool go = *(volatile uint32_t *)bad == 0;
+        if (tid == 0 && go) {
+            tc_fence_after();
+#pragma unroll
+            for (uint32_t h = 0; h < 2; ++h) {
+                const uint64_t da = tc_desc(smem_u32(Qs + h * (kAtRows * 128)));
+                const uint64_t db = tc_desc(smem_u32(Ks + h * (kAtKeys * 128)));
+#pragma unroll
+                for (uint32_t k = 0; k < 4; ++k) at_mma(tS, da + 2 * k, db + 2 * k, at_idesc(kAtKeys), (h | k) != 0);
+            }
+            tc_commit(&bar[0]);
+        }
+        if (go && !mbar_wait(&bar[0], it & 1u, err, ERR_WAIT_FULL)) atomicExch(bad, 1u);
+        tc_fence_after();
+        // this row's scores, mask, online softmax
+        float sc[64];
+        {
+            float a[32], b[32];
+            tc_ld32(tS + lane_off, a);
+            tc_ld32(tS + lane_off + 32, b);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) { sc[j] = a[j]; sc[32 + j] = b[j]; }
+        }
+        float mx = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 64; ++j) {
+            const uint32_t key = k0 + j;
+            sc[j] = (key <= pos && key < n_keys && live) ? __fmul_rn(sc[j], scale) : -INFINITY;
+            mx = fmaxf(mx, sc[j]);
+        }
+        const bool grow = mx > m_used + kAtRescale || (m_used == -INFINITY && mx != -INFINITY);
+        const float al = !grow ? 1.f : (m_used == -INFINITY ? 0.f : expf(m_used - mx));
+        if (grow) {
+            l *= al;
+            m_used = mx;
+        }
+        // O row *= al in TMEM (the previous PV MMA is complete); TMEM loads and
+        // stores are warp-wide, so a warp rescales when any of its rows grew
+        if (it > 0 && __any_sync(0xffffffffu, grow)) {
+#pragma unroll 1
+            for (uint32_t c0 = 0; c0 < 128; c0 += 32) {
+                float o[32];
+                tc_ld32(tO + lane_off + c0, o);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) o[j] *= al;
+                at_st32(tO + lane_off + c0, o);
+            }
+        }
+        float sum = 0.f;
+#pragma unroll
+        for (uint32_t c = 0; c < 8; ++c) {
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float pa = sc[8 * c + 2 * e] == -INFINITY ? 0.f : expf(sc[8 * c + 2 * e] - m_used);
+                const float pb = sc[8 * c + 2 * e + 1] == -INFINITY ? 0.f : expf(sc[8 * c + 2 * e + 1] - m_used);
+                const __half2 hp = __floats2half2_rn(pa, pb);
+                const float2 back = __half22float2(hp);
+                sum += back.x + back.y;
+                w[e] = *reinterpret_cast<const uint32_t *>(&hp);
+            }
+            *reinterpret_cast<uint4 *>(Ps + tc_sw128(r, c)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        l += sum;
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        tc_fence_before();
+        __syncthreads();
+        if (tid == 0 && *(volatile uint32_t *)bad == 0) {
+            tc_fence_after();
+            const uint64_t da = tc_desc(smem_u32(Ps)), db = tc_desc(smem_u32(Vt));
+#pragma unroll
+            for (uint32_t k = 0; k < 4; ++k) at_mma(tO, da + 2 * k, db + 2 * k, at_idesc(HD), (it | k) != 0);
+            tc_commit(&bar[1]);
+        }
+    }
+    // every MMA issued by thread 0 is covered by one more commit
+    if (tid == 0) tc_commit(&bar[2]);
+    const bool fin = mbar_wait(&bar[2], 0u, err, ERR_WAIT_DRAIN);
+    tc_fence_after();
+    if (__all_sync(0xffffffffu, fin && *(volatile uint32_t *)bad == 0) && n_tiles > 0) {  // warp-uniform
+        __half *dst = out + (size_t)tq * nq + (size_t)(kvh * GQ + r % GQ) * HD;
+        const float inv_ok = l;
+#pragma unroll 1
+        for (uint32_t c0 = 0; c0 < 128; c0 += 32) {
+            float o[32];
+            tc_ld32(tO + lane_off + c0, o);
+            if (live) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 2) {
+                    const __half2 hv = __floats2half2_rn(__fdiv_rn(o[j], inv_ok), __fdiv_rn(o[j + 1], inv_ok));
+                    *reinterpret_cast<__half2 *>(dst + c0 + j) = hv;
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256u) : "memory");
     }
 }
 

@@ -1553,6 +1553,17 @@ static bool launch_pf_attn(fwb_model *m, const float *kc, const float *vc, uint3
     const ModelConfig &c = m->cfg;
     const uint32_t H = c.n_head, KV = c.n_head_kv, hd = c.head_dim, gq = H / KV;
     const float scale = 1.0f / sqrtf((float)hd);
+    if (hd == kAtHd && (gq == 1 || gq == 2 || gq == 4 || gq == 8)) {  // tensor cores
+        const void *fn = gq == 1 ? (const void *)pf_attn_tc_kernel<1>
+                       : gq == 2 ? (const void *)pf_attn_tc_kernel<2>
+                       : gq == 4 ? (const void *)pf_attn_tc_kernel<4> : (const void *)pf_attn_tc_kernel<8>;
+        CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAtSmem));
+        const uint32_t QT = kAtRows / gq, nqt = (T + QT - 1) / QT;
+        void *args[] = {(void *)&m->pf_q, (void *)&kc, (void *)&vc, (void *)&T, (void *)&p0, (void *)&H,
+                        (void *)&m->kv_ctx, (void *)&scale, (void *)&m->pf_a16, (void *)&m->err};
+        CK(cudaLaunchKernel(fn, dim3(nqt, KV), dim3(kAtThreads), args, kAtSmem, st));
+        return true;
+    }
     if (hd == 128 || hd == 64) {
         switch (gq * 1000 + hd) {
         case 1128: return launch_pf_flash(m, (const void *)pf_flash_kernel<128, 1>, pf_flash_smem<128>(), 1, kc, vc, T, p0, scale, st);
