@@ -63,6 +63,20 @@ def test_prefill_q4_0_matches_oracle(gpu, tmp_path, n, pos0):
     _check(path, tokens, pos0, 4, 512)
 
 
+# the prompt attention's variants: tensor cores for head_dim 128 at query
+# groups 1, 4 and 8 (the 8B / 70B groups; group 2 is SMALL_Q4_0 above), the
+# CUDA-core flash kernel for head_dim 64, the per-(token, KV head) kernel for
+# other head dims; 150 tokens span several query and key tiles
+@pytest.mark.parametrize("n_embd,n_head,n_kv", [(1024, 8, 8), (1024, 8, 2), (1024, 8, 1), (512, 8, 2),
+                                                (256, 8, 4)])
+def test_prefill_attention_shapes(gpu, tmp_path, n_embd, n_head, n_kv):
+    cfg = dataclasses.replace(configs.SMALL_Q4_0, name=f"pf-{n_embd}-{n_head}-{n_kv}", n_embd=n_embd,
+                              n_head=n_head, n_head_kv=n_kv, n_ff=2 * n_embd)
+    path = gguf_synth.write_model(str(tmp_path / f"{cfg.name}.gguf"), cfg, seed=55)
+    tokens = np.random.default_rng(n_embd + n_kv).integers(0, cfg.n_vocab, 150)
+    _check(path, tokens, 0, 2, 512)
+
+
 def test_prefill_more_tokens_than_a_chunk(gpu, tmp_path):
     cfg = dataclasses.replace(configs.SMALL_Q4_0, name="small-q4_0-ctx1k", n_ctx=1024)
     path = gguf_synth.write_model(str(tmp_path / "pf1k.gguf"), cfg, seed=52)
