@@ -425,9 +425,11 @@ __global__ void __launch_bounds__(kPfThreads) pf_flash_kernel(const float *qf, c
 // heads of one KV head (row r: token r / GQ, head r % GQ) -- one row per
 // thread and TMEM lane, and walks the positions 0 .. p0 + (its last token)
 // in tiles of 64.  Per tile:
-//  * the K tile (64 x 128) and the V tile are rounded to fp16 into shared
-//    memory in the K-major 128-byte-swizzled layout (V transposed: dims x
-//    positions), q once per block the same way (two 64-dim halves);
+//  * the K tile (64 x 128) and the V tile, rounded to fp16 once per layer by
+//    pf_kv16_kernel (V transposed: dims x positions), arrive by 16-byte
+//    cp.async copies into the K-major 128-byte-swizzled layout, double
+//    buffered: tile t+1 is in flight while tile t computes; q is rounded to
+//    fp16 once per block the same way (two 64-dim halves);
 //  * one thread issues S = q k^T as tcgen05.mma.kind::f16 (M 128, N 64,
 //    K 8 x 16; fp32 in TMEM columns 0..63) and commits to an mbarrier;
 //  * each thread reads its row's 64 scores (tcgen05.ld), scales by
@@ -449,8 +451,42 @@ constexpr uint32_t kAtQBytes = kAtRows * kAtHd * 2;   // two 64-dim halves of 16
 constexpr uint32_t kAtKBytes = kAtKeys * kAtHd * 2;   // two halves of 8 KB
 constexpr uint32_t kAtVBytes = kAtHd * kAtKeys * 2;   // 128 dims x 64 positions
 constexpr uint32_t kAtPBytes = kAtRows * kAtKeys * 2; // 128 rows x 64 positions
-constexpr uint32_t kAtSmem = kAtQBytes + kAtKBytes + kAtVBytes + kAtPBytes + 1024 + 128;
+constexpr uint32_t kAtSmem = kAtQBytes + 2 * (kAtKBytes + kAtVBytes) + kAtPBytes + 1024 + 128;  // K, V twice
 constexpr float kAtRescale = 5.0f;
+
+// The layer's K and V rows 0 .. n_pos-1 rounded to fp16 once, for every
+// query tile of the tensor-core attention: K16[kv][pos][128] and V
+// transposed, Vt16[kv][dim][pos] (row stride ctx_pad, a multiple of 64);
+// positions n_pos .. the end of the last 64-row tile are zeros.  Grid
+// (ceil(n_pos / 64), n_kv), 256 threads; the transpose goes through shared
+// memory so that both writes are coalesced.
+__global__ void __launch_bounds__(256) pf_kv16_kernel(const float *kcache, const float *vcache, uint32_t n_pos,
+                                                      uint32_t kv_ctx, uint32_t ctx_pad, __half *k16,
+                                                      __half *vt16) {
+    __shared__ float vs[64][129];
+    const uint32_t j0 = blockIdx.x * 64, kvh = blockIdx.y, tid = threadIdx.x;
+    const float *kb = kcache + (size_t)kvh * kv_ctx * 128, *vb = vcache + (size_t)kvh * kv_ctx * 128;
+    __half *kd = k16 + (size_t)kvh * ctx_pad * 128, *vd = vt16 + (size_t)kvh * 128 * ctx_pad;
+    for (uint32_t i = tid; i < 64 * 32; i += 256) {
+        const uint32_t r = i >> 5, c4 = i & 31, j = j0 + r;
+        float4 k = make_float4(0.f, 0.f, 0.f, 0.f), v = k;
+        if (j < n_pos) {
+            k = *reinterpret_cast<const float4 *>(kb + (size_t)j * 128 + 4 * c4);
+            v = *reinterpret_cast<const float4 *>(vb + (size_t)j * 128 + 4 * c4);
+        }
+        *reinterpret_cast<uint2 *>(kd + (size_t)j * 128 + 4 * c4) = make_uint2(pack_h2(k.x, k.y), pack_h2(k.z, k.w));
+        vs[r][4 * c4] = v.x; vs[r][4 * c4 + 1] = v.y; vs[r][4 * c4 + 2] = v.z; vs[r][4 * c4 + 3] = v.w;
+    }
+    __syncthreads();
+    // warp w writes dims 16 w .. 16 w + 15; lane l the positions 2 l, 2 l + 1 of each
+    const uint32_t warp = tid >> 5, lane = tid & 31;
+#pragma unroll 4
+    for (uint32_t i = 0; i < 16; ++i) {
+        const uint32_t d = warp * 16 + i;
+        *reinterpret_cast<uint32_t *>(vd + (size_t)d * ctx_pad + j0 + 2 * lane) =
+            pack_h2(vs[2 * lane][d], vs[2 * lane + 1][d]);
+    }
+}
 
 __device__ __forceinline__ void at_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                        uint32_t acc) {
@@ -485,15 +521,15 @@ __device__ __forceinline__ void at_st32(uint32_t taddr, const float (&v)[32]) {
 }
 
 template <int GQ>
-__global__ void __launch_bounds__(kAtThreads) pf_attn_tc_kernel(const float *qf, const float *kcache,
-                                                                const float *vcache, uint32_t T, uint32_t p0,
-                                                                uint32_t n_head, uint32_t kv_ctx, float scale,
+__global__ void __launch_bounds__(kAtThreads) pf_attn_tc_kernel(const float *qf, const __half *k16,
+                                                                const __half *vt16, uint32_t T, uint32_t p0,
+                                                                uint32_t n_head, uint32_t ctx_pad, float scale,
                                                                 __half *out, uint32_t *err) {
     constexpr uint32_t QT = kAtRows / GQ, HD = kAtHd;
     extern __shared__ uint8_t at_smem_raw[];
     const uint32_t base = (smem_u32(at_smem_raw) + 1023u) & ~1023u;
     uint8_t *sm = at_smem_raw + (base - smem_u32(at_smem_raw));
-    uint8_t *Qs = sm, *Ks = Qs + kAtQBytes, *Vt = Ks + kAtKBytes, *Ps = Vt + kAtVBytes;
+    uint8_t *Qs = sm, *Kb = Qs + kAtQBytes, *Vb = Kb + 2 * kAtKBytes, *Ps = Vb + 2 * kAtVBytes;
     uint64_t *bar = reinterpret_cast<uint64_t *>(Ps + kAtPBytes);  // [0] S done, [1] PV done, [2] final
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar + 3);
     uint32_t *bad = tmem_slot + 1;
@@ -501,7 +537,22 @@ __global__ void __launch_bounds__(kAtThreads) pf_attn_tc_kernel(const float *qf,
     const uint32_t nq = n_head * HD, nqt = (T + QT - 1) / QT;
     const uint32_t qt = nqt - 1 - blockIdx.x;  // the longest key ranges start first
     const uint32_t t0 = qt * QT;
-    const float *kb = kcache + (size_t)kvh * kv_ctx * HD, *vb = vcache + (size_t)kvh * kv_ctx * HD;
+    const __half *kg = k16 + (size_t)kvh * ctx_pad * HD, *vg = vt16 + (size_t)kvh * HD * ctx_pad;
+    // 16-byte asynchronous copies of key tile `it` into buffer it & 1, placed in
+    // the swizzled layouts: K rows (two 64-dim halves), V^T rows (dims)
+    auto fetch_tile = [&](uint32_t it) {
+        const uint32_t k0 = it * kAtKeys, b = it & 1u;
+        uint8_t *Ks = Kb + b * kAtKBytes, *Vt = Vb + b * kAtVBytes;
+#pragma unroll
+        for (uint32_t q = 0; q < 8; ++q) {
+            const uint32_t i = tid + q * kAtThreads;  // 1024 chunks of each
+            const uint32_t j = i >> 4, c = i & 15;     // K: row j, 16-byte chunk c of its 128 dims
+            cp_async16(Ks + (c >> 3) * (kAtKeys * 128) + tc_sw128(j, c & 7), kg + (size_t)(k0 + j) * HD + 8 * c);
+            const uint32_t d = i >> 3, e = i & 7;      // V^T: row d, chunk e of its 64 positions
+            cp_async16(Vt + tc_sw128(d, e), vg + (size_t)d * ctx_pad + k0 + 8 * e);
+        }
+        cp_async_commit();
+    };
 
     if (tid == 0) {
         for (int i = 0; i < 3; ++i) mbar_init(&bar[i], 1);
@@ -542,35 +593,19 @@ __global__ void __launch_bounds__(kAtThreads) pf_attn_tc_kernel(const float *qf,
     const uint32_t n_keys = p0 + t_last + 1, n_tiles = (n_keys + kAtKeys - 1) / kAtKeys;
     const uint32_t pos = p0 + tq;
     float m_used = -INFINITY, l = 0.f;
+    fetch_tile(0);
     for (uint32_t it = 0; it < n_tiles; ++it) {
         const uint32_t k0 = it * kAtKeys;
-        // the previous tile's MMAs are done with K, V, P and O
+        uint8_t *Ks = Kb + (it & 1u) * kAtKBytes, *Vt = Vb + (it & 1u) * kAtVBytes;
+        // the previous tile's MMAs are done with its K / V buffer (the next
+        // tile's), P and O
         if (it > 0 && !mbar_wait(&bar[1], (it - 1) & 1u, err, ERR_WAIT_FULL)) atomicExch(bad, 1u);
         tc_fence_after();
-        {  // K and V rows of this tile -> fp16: thread t takes position t / 2, dims [64 (t & 1), +64)
-            const uint32_t j = tid >> 1, h = tid & 1, key = k0 + j;
-            const bool in = key < n_keys;
-            const float *kr = kb + (size_t)key * HD + 64 * h, *vr = vb + (size_t)key * HD + 64 * h;
-#pragma unroll 2
-            for (uint32_t c = 0; c < 8; ++c) {
-                float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a, va = a, vb4 = a;
-                if (in) {
-                    a = *reinterpret_cast<const float4 *>(kr + 8 * c);
-                    b = *reinterpret_cast<const float4 *>(kr + 8 * c + 4);
-                    va = *reinterpret_cast<const float4 *>(vr + 8 * c);
-                    vb4 = *reinterpret_cast<const float4 *>(vr + 8 * c + 4);
-                }
-                uint4 o;
-                o.x = pack_h2(a.x, a.y); o.y = pack_h2(a.z, a.w); o.z = pack_h2(b.x, b.y); o.w = pack_h2(b.z, b.w);
-                *reinterpret_cast<uint4 *>(Ks + h * (kAtKeys * 128) + tc_sw128(j, c)) = o;
-                // V transposed: row = dimension, K index = position j
-                const float vv[8] = {va.x, va.y, va.z, va.w, vb4.x, vb4.y, vb4.z, vb4.w};
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const uint32_t d = 64 * h + 8 * c + e;
-                    *reinterpret_cast<__half *>(Vt + tc_sw128(d, j >> 3) + 2 * (j & 7)) = __float2half_rn(vv[e]);
-                }
-            }
+        if (it + 1 < n_tiles) {
+            fetch_tile(it + 1);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");  // this thread's copies of tile it
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         tc_fence_before();

@@ -477,6 +477,8 @@ struct fwb_model {
     uint32_t *pf_tok = nullptr;
     float *pf_x = nullptr, *pf_qkv = nullptr, *pf_q = nullptr, *pf_g = nullptr, *pf_u = nullptr;
     __half *pf_h16 = nullptr, *pf_a16 = nullptr;
+    __half *pf_k16 = nullptr, *pf_vt16 = nullptr;  // a layer's K / transposed V in fp16 (tensor-core attention)
+    uint32_t pf_ctx_pad = 0;
 };
 
 namespace fwb {
@@ -1531,6 +1533,11 @@ static bool prefill_alloc(fwb_model *m) {
         !dalloc(m, (void **)&m->pf_g, C * F * 4) || !dalloc(m, (void **)&m->pf_u, C * F * 4) ||
         !dalloc(m, (void **)&m->pf_h16, C * W16 * 2) || !dalloc(m, (void **)&m->pf_a16, C * NQ * 2))
         return false;
+    if (c.head_dim == kAtHd) {
+        m->pf_ctx_pad = (m->kv_ctx + 63) / 64 * 64;
+        const size_t n16 = (size_t)c.n_head_kv * m->pf_ctx_pad * kAtHd;
+        if (!dalloc(m, (void **)&m->pf_k16, n16 * 2) || !dalloc(m, (void **)&m->pf_vt16, n16 * 2)) return false;
+    }
     m->pf_cap = (uint32_t)C;
     return true;
 }
@@ -1553,14 +1560,18 @@ static bool launch_pf_attn(fwb_model *m, const float *kc, const float *vc, uint3
     const ModelConfig &c = m->cfg;
     const uint32_t H = c.n_head, KV = c.n_head_kv, hd = c.head_dim, gq = H / KV;
     const float scale = 1.0f / sqrtf((float)hd);
-    if (hd == kAtHd && (gq == 1 || gq == 2 || gq == 4 || gq == 8)) {  // tensor cores
+    if (hd == kAtHd && (gq == 1 || gq == 2 || gq == 4 || gq == 8) && m->pf_k16) {  // tensor cores
+        const uint32_t n_pos = p0 + T;
+        pf_kv16_kernel<<<dim3((n_pos + 63) / 64, KV), 256, 0, st>>>(kc, vc, n_pos, m->kv_ctx, m->pf_ctx_pad,
+                                                                   m->pf_k16, m->pf_vt16);
         const void *fn = gq == 1 ? (const void *)pf_attn_tc_kernel<1>
                        : gq == 2 ? (const void *)pf_attn_tc_kernel<2>
                        : gq == 4 ? (const void *)pf_attn_tc_kernel<4> : (const void *)pf_attn_tc_kernel<8>;
         CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAtSmem));
         const uint32_t QT = kAtRows / gq, nqt = (T + QT - 1) / QT;
-        void *args[] = {(void *)&m->pf_q, (void *)&kc, (void *)&vc, (void *)&T, (void *)&p0, (void *)&H,
-                        (void *)&m->kv_ctx, (void *)&scale, (void *)&m->pf_a16, (void *)&m->err};
+        const __half *k16 = m->pf_k16, *vt16 = m->pf_vt16;
+        void *args[] = {(void *)&m->pf_q, (void *)&k16, (void *)&vt16, (void *)&T, (void *)&p0, (void *)&H,
+                        (void *)&m->pf_ctx_pad, (void *)&scale, (void *)&m->pf_a16, (void *)&m->err};
         CK(cudaLaunchKernel(fn, dim3(nqt, KV), dim3(kAtThreads), args, kAtSmem, st));
         return true;
     }
