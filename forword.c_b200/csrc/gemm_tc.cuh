@@ -53,6 +53,7 @@ enum TcMode : uint32_t { TC_STORE = 0, TC_ADD = 1 };
 
 struct TcArgs {
     CUtensorMap xmap;     // the activations as a 2-D tensor map: box 64 x 128, 128-byte swizzle
+    CUtensorMap wmap;     // F16W: the weights already expanded to fp16 [N][K], the same box and swizzle
     const uint8_t *w;     // Q4_0 rows [N][K/32 blocks]
     uint32_t row_bytes;   // K/32 * 18
     const __half *x;      // [M][K] fp16, row-major
@@ -188,7 +189,33 @@ __device__ __forceinline__ void tc_fetch_w(const TcArgs &a, uint32_t n, uint32_t
     }
 }
 
-template <bool V16>
+// Q4_0 rows [rows][cols] -> fp16 [rows][cols]: (q - 8) * d rounded once to
+// fp16 (the fp32 product of the 4-bit integer and the fp16 scale is exact),
+// the same values the producers of gemm_q4_0_tc_kernel write into the B
+// tile.  One thread per 32-value block.
+__global__ void q4_0_to_f16_kernel(const uint8_t *w, uint64_t n_blocks, __half *out) {
+    for (uint64_t b = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; b < n_blocks;
+         b += (uint64_t)gridDim.x * blockDim.x) {
+        const uint8_t *blk = w + b * 18;
+        const float d = __half2float(__ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8))));
+        uint4 o[4];
+        uint32_t *ow = reinterpret_cast<uint32_t *>(o);
+#pragma unroll
+        for (int j = 0; j < 16; j += 2) {
+            const uint32_t q0 = blk[2 + j], q1 = blk[3 + j];
+            ow[j / 2] = pack_h2((float)((int)(q0 & 15) - 8) * d, (float)((int)(q1 & 15) - 8) * d);
+            ow[8 + j / 2] = pack_h2((float)((int)(q0 >> 4) - 8) * d, (float)((int)(q1 >> 4) - 8) * d);
+        }
+        uint4 *dst = reinterpret_cast<uint4 *>(out + b * 32);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dst[i] = o[i];
+    }
+}
+
+// V16: the Q4_0 rows allow 16-byte loads.  F16W: the weights come as fp16
+// through wmap (expanded once by q4_0_to_f16_kernel): the TMA thread loads
+// both operands of every stage and the producer warps only run the epilogue.
+template <bool V16, bool F16W = false>
 __global__ void __launch_bounds__(kTcThreads, 2) gemm_q4_0_tc_kernel(const __grid_constant__ TcArgs a) {
     extern __shared__ uint8_t tc_smem_raw[];
     const uint32_t base = (smem_u32(tc_smem_raw) + 1023u) & ~1023u;
@@ -227,7 +254,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) gemm_q4_0_tc_kernel(const __gri
             uint32_t i = 0;
             for (; i < steps; ++i) {
                 const uint32_t s = i % kTcStages;
-                if (!mbar_wait(&full[s], (i / kTcStages) & 1u, a.err, ERR_WAIT_FULL) ||
+                if ((!F16W && !mbar_wait(&full[s], (i / kTcStages) & 1u, a.err, ERR_WAIT_FULL)) ||
                     !mbar_wait(&afull[s], (i / kTcStages) & 1u, a.err, ERR_WAIT_FULL)) {
                     ok = false;
                     break;
@@ -247,14 +274,16 @@ __global__ void __launch_bounds__(kTcThreads, 2) gemm_q4_0_tc_kernel(const __gri
         // ---- activation tiles by TMA: one thread
         if (lane == 0) {
             asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&a.xmap)) : "memory");
+            if (F16W) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&a.wmap)) : "memory");
             uint32_t i = 0;
             for (; i < steps; ++i) {
                 const uint32_t s = i % kTcStages;
                 if (i >= kTcStages &&
                     !mbar_wait(&empty[s], ((i / kTcStages) - 1) & 1u, a.err, ERR_WAIT_EMPTY))
                     break;
-                mbar_arrive_expect_tx(&afull[s], kTcTileBytes);
+                mbar_arrive_expect_tx(&afull[s], F16W ? 2 * kTcTileBytes : kTcTileBytes);
                 tc_tma_x(smem + s * 2u * kTcTileBytes, &a.xmap, i * kTcK, m0, &afull[s]);
+                if (F16W) tc_tma_x(smem + s * 2u * kTcTileBytes + kTcTileBytes, &a.wmap, i * kTcK, n0, &afull[s]);
             }
             // before the CTA may exit, the copies still in flight land (the
             // MMA thread consumed every stage unless a wait failed)
@@ -266,8 +295,8 @@ __global__ void __launch_bounds__(kTcThreads, 2) gemm_q4_0_tc_kernel(const __gri
         // ---- producers: thread t fills weight row t of each stage
         const uint32_t t = tid, n = n0 + t;
         uint32_t wc[36];
-        if (steps) tc_fetch_w<V16>(a, n, 0, steps, wc);
-        for (uint32_t c0 = 0; c0 < steps && ok; c0 += 4) {
+        if (steps && !F16W) tc_fetch_w<V16>(a, n, 0, steps, wc);
+        for (uint32_t c0 = 0; c0 < steps && ok && !F16W; c0 += 4) {
             uint32_t wn[36];
             tc_fetch_w<V16>(a, n, c0 + 4, steps, wn);  // zeros past the last step
 #pragma unroll

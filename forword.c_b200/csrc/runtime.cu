@@ -478,6 +478,8 @@ struct fwb_model {
     float *pf_x = nullptr, *pf_qkv = nullptr, *pf_q = nullptr, *pf_g = nullptr, *pf_u = nullptr;
     __half *pf_h16 = nullptr, *pf_a16 = nullptr;
     __half *pf_k16 = nullptr, *pf_vt16 = nullptr;  // a layer's K / transposed V in fp16 (tensor-core attention)
+    // the prompt GEMMs' weights expanded to fp16 once (qkv, o, gate, up, down per layer), or empty
+    std::vector<__half *> pf_w16;
     uint32_t pf_ctx_pad = 0;
 };
 
@@ -1294,7 +1296,8 @@ static decltype(&cuTensorMapEncodeTiled) tensor_map_encoder() {
 // = W X[m] for m < M, or += with TC_ADD.  Q4_0 with K a multiple of 64,
 // 4-byte-aligned weights and 16-byte-aligned fp16 activations only.
 static bool launch_tc_gemm(const void *w, size_t w_bytes, uint32_t type, const void *x, float *y, size_t K, size_t N,
-                           size_t M, size_t ldy, uint32_t mode, cudaStream_t st, uint32_t *err) {
+                           size_t M, size_t ldy, uint32_t mode, cudaStream_t st, uint32_t *err,
+                           const __half *w16 = nullptr) {
     static bool attr_set[64] = {};
     if (!w || !x || !y || !K || !N || !M) { set_err("quant_gemm: null pointer or zero size"); return false; }
     if (type != 2) { set_err("quant_gemm: only Q4_0 (type 2) runs on the tensor cores"); return false; }
@@ -1310,6 +1313,8 @@ static bool launch_tc_gemm(const void *w, size_t w_bytes, uint32_t type, const v
                                 (int)kTcSmem));
         CK(cudaFuncSetAttribute((const void *)gemm_q4_0_tc_kernel<false>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem));
+        CK(cudaFuncSetAttribute((const void *)gemm_q4_0_tc_kernel<false, true>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem));
         attr_set[dev] = true;
     }
     TcArgs a{};
@@ -1323,6 +1328,13 @@ static bool launch_tc_gemm(const void *w, size_t w_bytes, uint32_t type, const v
                                estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (r != CUDA_SUCCESS) { set_err("quant_gemm: activation tensor map rejected"); return false; }
+        if (w16) {  // the fp16 copy of the weights [N][K], the same boxes
+            const cuuint64_t wdims[2] = {(cuuint64_t)K, (cuuint64_t)N};
+            const CUresult rw = enc(&a.wmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half *>(w16), wdims,
+                                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+            if (rw != CUDA_SUCCESS) { set_err("quant_gemm: weight tensor map rejected"); return false; }
+        }
     }
     a.w = static_cast<const uint8_t *>(w);
     a.row_bytes = (uint32_t)row_bytes;
@@ -1335,7 +1347,9 @@ static bool launch_tc_gemm(const void *w, size_t w_bytes, uint32_t type, const v
     a.mode = mode;
     a.err = err;
     const dim3 grid((unsigned)((N + kTcN - 1) / kTcN), (unsigned)((M + kTcM - 1) / kTcM));
-    if (row_bytes % 16 == 0 && (uintptr_t)w % 16 == 0)  // 16-byte weight loads
+    if (w16)
+        gemm_q4_0_tc_kernel<false, true><<<grid, kTcThreads, kTcSmem, st>>>(a);
+    else if (row_bytes % 16 == 0 && (uintptr_t)w % 16 == 0)  // 16-byte weight loads
         gemm_q4_0_tc_kernel<true><<<grid, kTcThreads, kTcSmem, st>>>(a);
     else
         gemm_q4_0_tc_kernel<false><<<grid, kTcThreads, kTcSmem, st>>>(a);
@@ -1533,6 +1547,24 @@ static bool prefill_alloc(fwb_model *m) {
         !dalloc(m, (void **)&m->pf_g, C * F * 4) || !dalloc(m, (void **)&m->pf_u, C * F * 4) ||
         !dalloc(m, (void **)&m->pf_h16, C * W16 * 2) || !dalloc(m, (void **)&m->pf_a16, C * NQ * 2))
         return false;
+    {  // fp16 copies of the layer weights for the prompt GEMMs, if they fit with room to spare
+        size_t need = 0;
+        for (const LayerW &w : m->layers)
+            for (const Mat *t : {&w.qkv, &w.o, &w.gate, &w.up, &w.down}) need += (size_t)t->rows * t->cols * 2;
+        size_t free_b = 0, total_b = 0;
+        if (cudaMemGetInfo(&free_b, &total_b) == cudaSuccess && free_b > need + ((size_t)8 << 30)) {
+            for (const LayerW &w : m->layers)
+                for (const Mat *t : {&w.qkv, &w.o, &w.gate, &w.up, &w.down}) {
+                    __half *p16 = nullptr;
+                    if (!dalloc(m, (void **)&p16, (size_t)t->rows * t->cols * 2)) return false;
+                    const uint64_t nb = (uint64_t)t->rows * t->cols / 32;
+                    q4_0_to_f16_kernel<<<(unsigned)std::min<uint64_t>(4096, (nb + 255) / 256), 256, 0, m->st>>>(
+                        t->p, nb, p16);
+                    m->pf_w16.push_back(p16);
+                }
+            CK(cudaGetLastError());
+        }
+    }
     if (c.head_dim == kAtHd) {
         m->pf_ctx_pad = (m->kv_ctx + 63) / 64 * 64;
         const size_t n16 = (size_t)c.n_head_kv * m->pf_ctx_pad * kAtHd;
@@ -1628,27 +1660,29 @@ static bool prefill_chunk(fwb_model *m, const uint32_t *tokens, uint32_t T, uint
     for (uint32_t l = 0; l < c.n_layer; ++l) {
         const LayerW &w = m->layers[l];
         float *kc = m->kc + l * layer_kv, *vc = m->vc + l * layer_kv;
+        // the layer's fp16 weight copies (qkv, o, gate, up, down), when the model has them
+        auto w16 = [&](int i) -> const __half * { return m->pf_w16.empty() ? nullptr : m->pf_w16[5 * l + i]; };
         pf_rmsnorm_f16_kernel<<<T, 256, 0, st>>>(m->pf_x, w.attn_norm, c.norm_eps, E, m->pf_h16);
         if (!launch_tc_gemm(w.qkv.p, (size_t)w.qkv.rows * w.qkv.row_bytes, 2, m->pf_h16, m->pf_qkv, E, NQKV, T, NQKV,
-                            TC_STORE, st, m->err))
+                            TC_STORE, st, m->err, w16(0)))
             return false;
         pf_rope_kv_kernel<<<T, 256, 0, st>>>(m->pf_qkv, p0, NQ, NKV, hd, m->rope_cos, m->rope_sin, m->pf_q, kc, vc,
                                              m->kv_ctx);
         if (!launch_pf_attn(m, kc, vc, T, p0, att_smem, st)) return false;
         if (l + 1 == c.n_layer) break;  // the last layer's output feeds only the logits
         if (!launch_tc_gemm(w.o.p, (size_t)w.o.rows * w.o.row_bytes, 2, m->pf_a16, m->pf_x, NQ, E, T, E, TC_ADD, st,
-                            m->err))
+                            m->err, w16(1)))
             return false;
         pf_rmsnorm_f16_kernel<<<T, 256, 0, st>>>(m->pf_x, w.ffn_norm, c.norm_eps, E, m->pf_h16);
         if (!launch_tc_gemm(w.gate.p, (size_t)w.gate.rows * w.gate.row_bytes, 2, m->pf_h16, m->pf_g, E, F, T, F,
-                            TC_STORE, st, m->err) ||
+                            TC_STORE, st, m->err, w16(2)) ||
             !launch_tc_gemm(w.up.p, (size_t)w.up.rows * w.up.row_bytes, 2, m->pf_h16, m->pf_u, E, F, T, F, TC_STORE,
-                            st, m->err))
+                            st, m->err, w16(3)))
             return false;
         pf_swiglu_kernel<<<std::min<size_t>(4 * 148, ((size_t)T * F / 4 + 255) / 256), 256, 0, st>>>(
             m->pf_g, m->pf_u, (size_t)T * F, m->pf_h16);
         if (!launch_tc_gemm(w.down.p, (size_t)w.down.rows * w.down.row_bytes, 2, m->pf_h16, m->pf_x, F, E, T, E,
-                            TC_ADD, st, m->err))
+                            TC_ADD, st, m->err, w16(4)))
             return false;
     }
     cudaError_t e = cudaGetLastError();
