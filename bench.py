@@ -386,7 +386,8 @@ def run_b200(args) -> None:
         prefill = {"tokens": P, "ms": pf_s * 1e3, "tokens_per_s": P / pf_s,
                    "gemm_tflops": flops / pf_s / 1e12,
                    "api": "fwb_prefill with host tokens and the last token's host logits (wall clock): "
-                          "P-1 tokens through the tensor-core dequant-GEMM path, the last through the decode step"}
+                          "P-1 tokens through the tensor-core path (GEMMs on fp16 weight copies made at the first "
+                          "call, tcgen05 attention), the last through the decode step"}
     else:
         tok = 0
         for i, t in enumerate(prompt):
