@@ -27,7 +27,10 @@
 //    refilling the stage.
 // After the last MMA a commit to `done` releases the epilogue: the producer
 // warps read the accumulator with tcgen05.ld (warp w owns TMEM lanes
-// 32w..32w+31) and store, or add into, Y.
+// 32w..32w+31) and store, or add into, Y.  The F16W instance takes weights
+// already expanded to fp16 (q4_0_to_f16_kernel, the same values): the TMA
+// thread then loads both tiles of a stage and the producers only run the
+// epilogue.
 //
 // Numerics: fp16 weights carry (q - 8) * d to 11 significant bits and fp16
 // activations x to 11 bits; products and sums are fp32.  Every wait is

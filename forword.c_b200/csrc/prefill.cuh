@@ -7,7 +7,8 @@
 // around them, with the same arithmetic as the decode step (rms_norm,
 // norm.c:7-16; RoPE, rope.c:28-53; causal softmax attention,
 // attention.c:142-164; SwiGLU, ffn.c:17-25,82-106).  Activations that feed a
-// GEMM are rounded to fp16; everything else is fp32.
+// GEMM are rounded to fp16, and so are q, k, v and the probabilities in the
+// tensor-core attention (head_dim 128); everything else is fp32.
 #pragma once
 #include "common.cuh"
 #include "gemm_tc.cuh"
